@@ -1,0 +1,154 @@
+/* qvl_b200.h -- C ABI of the B200 (sm_100a) INT8 hot path of the Qwen3-VL-2B
+ * inference engine (drop-in for dangtruong-github/qwen3-vl-2b-inference's
+ * matmul/ INT8 kernels, SwiGLU MLP and GQA attention).
+ *
+ * Conventions for every entry point
+ *   - All tensor pointers are DEVICE pointers unless the name ends in _host.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Calls are asynchronous on `stream`; they return a status code and never
+ *     call exit() or trap.  The reference's error convention (fprintf + exit(1)
+ *     on an unsupported dtype combination, matmul/src/cpu_wrapper.cpp:394-395)
+ *     is kept only by the C++ `linear()` shim in qvl_b200_linear.hpp.
+ *   - Nothing allocates device memory on the hot path: scratch is a caller-
+ *     provided `workspace` whose size the matching *_workspace_bytes()
+ *     function reports.
+ *   - Weights use the reference's packed layout unchanged
+ *     (export_bin/export_qwen_bin.py:242-275, 297-357): int8 row-major [N, K]
+ *     (HF [out, in]); fp32 scales [N * K / group_size] with row n, group gi at
+ *     n * (K / group_size) + gi.  Per-output-row quantisation is
+ *     group_size == K.
+ */
+#ifndef QVL_B200_H
+#define QVL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define QVL_OK 0
+#define QVL_ERR_INVALID 1       /* bad pointer, size or alignment            */
+#define QVL_ERR_UNSUPPORTED 2   /* shape/dtype combination not implemented    */
+#define QVL_ERR_CUDA 3          /* a CUDA runtime call failed                  */
+#define QVL_ERR_WORKSPACE 4     /* workspace missing or too small              */
+
+/* Reference dtype enum (utils/include/tensor.hpp:25-27), same values. */
+#define QVL_DTYPE_FP32 0
+#define QVL_DTYPE_INT32 1
+#define QVL_DTYPE_FP16 2
+#define QVL_DTYPE_INT8 3
+#define QVL_DTYPE_INT4 4
+
+/* Floating-point summation semantics of the INT8 products.
+ * The integer group sums are exact in all modes; the modes differ only in how
+ * the fp32 result is assembled from them, mirroring the reference kernels:
+ *   QVL_SEM_REFERENCE: what f32a_i8f32sb_f32c_avx2_kernel does for this shape
+ *       (cpu_f32a_i8f32sb_f32c_avx2.cpp:464-475): LANE8 when M == 1 &&
+ *       N >= 1024 && K >= 1024, TILED otherwise.
+ *   QVL_SEM_LANE8: every row is an independent M=1 decode GEMV (:122-224 and
+ *       :327-455): 8 int32 lanes per group (k mod 16 in {2l, 2l+1}), each lane
+ *       fused into an fp32 lane accumulator, lanes reduced (l, l+4) pairwise.
+ *       Use this for a batch of independent decode requests.
+ *   QVL_SEM_TILED: the M>1 kernel (:538-653): per group the whole int32 sum
+ *       is converted and accumulated as fma(float(S) * a_s, w_s, acc). */
+#define QVL_SEM_REFERENCE 0
+#define QVL_SEM_LANE8 1
+#define QVL_SEM_TILED 2
+
+const char *qvl_status_string(int status);
+/* Last CUDA error code recorded by a QVL_ERR_CUDA return (0 if none). */
+int qvl_last_cuda_error(void);
+/* Library version, e.g. "qvl_b200 0.1". */
+const char *qvl_version(void);
+
+/* ---- activation quantisation (inlined in every reference INT8 kernel,
+ *      cpu_f32a_i8f32sb_f32c_avx2.cpp:135-177, :348-390, :488-530) ---------
+ * x fp32 [M, K] -> q int16 [M, K], q_scales fp32 [M, K / group_size]:
+ * s = sqrtf(sum(x^2) / g + 1e-6) / 127 per group, q = sat16(rne(x / s)).
+ * Requires K % group_size == 0 and group_size % 16 == 0. */
+int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales,
+                      size_t M, size_t K, size_t group_size, void *stream);
+
+/* ---- INT8 linear: C[M,N] = A[M,K] . dequant(B[N,K])^T, fp32 in/out -------
+ * Replaces linear()'s INT8 branch (matmul/src/cpu_wrapper.cpp:339-357) and
+ * the kernels behind it (f32a_i8f32sb_f32c_avx2_kernel,
+ * matmul/src/cpu_f32a_i8f32sb_f32c_avx2.cpp:665-702).
+ * group_quantized == 0 means per-output-row scales (group_size := K); the
+ * reference's own row-quant branch reads B as [K, N] (cpu_wrapper.cpp:172-215)
+ * and is not reproduced.  Workspace holds the quantised activations. */
+size_t qvl_linear_i8_workspace_bytes(size_t M, size_t K, size_t group_size);
+int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float *C,
+                  size_t M, size_t N, size_t K, int group_quantized, size_t group_size,
+                  int semantics, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Same product from already-quantised activations (qvl_quantize_rows output),
+ * so q/k/v or gate/up share one quantisation of their common input. */
+int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
+                      const float *B_scales, float *C, size_t M, size_t N, size_t K,
+                      size_t group_size, int semantics, void *stream);
+
+/* ---- SwiGLU (layers/src/text_layer.cpp:420-434) ------------------------
+ * gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i], in place, n elements. */
+int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);
+
+/* Fused MLP chain: out[M,H] = down(swiglu(gate(x), up(x))), the sequence of
+ * model/src/forward.cpp:621-654 (gate/up linear, swiglu, down linear).
+ * Wg, Wu: int8 [I, H]; Wd: int8 [H, I]; scales in the reference layout.
+ * Workspace: qvl_swiglu_mlp_workspace_bytes(M, H, I, group_size). */
+size_t qvl_swiglu_mlp_workspace_bytes(size_t M, size_t H, size_t I, size_t group_size);
+int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg,
+                      const int8_t *Wu, const float *su, const int8_t *Wd,
+                      const float *sd, float *out, size_t M, size_t H, size_t I,
+                      size_t group_size, int semantics, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* ---- GQA attention over a paged FP16 KV cache --------------------------
+ * Replaces apply_rotary / apply_rotary_cache / the v-cache copy
+ * (layers/src/text_layer.cpp:712-824, model/src/forward.cpp:545-562) and
+ * attn_scores_all_heads + softmax + attn_weighted_sum_all_heads
+ * (layers/src/text_layer.cpp:436-710).
+ *
+ * KV layout (per layer): k_pages, v_pages fp16 [num_pages, NKV, page_size, D].
+ * page_table int32 [num_seqs, max_pages_per_seq]: logical page p of sequence s
+ * lives at physical page page_table[s * max_pages_per_seq + p].
+ * Query i belongs to sequence seq_ids[i] at position positions[i] and attends
+ * causally over positions [0, positions[i]].
+ * rope_cos/rope_sin fp32 [max_pos, D/2]: the text section of the reference's
+ * table (model/src/load_model.cpp:413-490), computed on the host.
+ *
+ * qvl_rope_kv_append: q fp32 [nq, NH, D] rotated in place; k_new, v_new fp32
+ * [nq, NKV, D]: k rotated, both rounded to fp16 and written at their position.
+ * qvl_attention_decode: out fp32 [nq, NH, D]. */
+typedef struct {
+    int num_heads;          /* NH  (16 for Qwen3-VL-2B)                 */
+    int num_kv_heads;       /* NKV (8)                                  */
+    int head_dim;           /* D   (128; only 128 is implemented)       */
+    int page_size;          /* tokens per page (multiple of 16)         */
+    int max_pages_per_seq;  /* row stride of page_table                 */
+    int max_pos;            /* rows of rope_cos / rope_sin              */
+} qvl_attn_dims;
+
+int qvl_rope_kv_append(float *q, const float *k_new, const float *v_new,
+                       uint16_t *k_pages, uint16_t *v_pages, const int32_t *page_table,
+                       const int32_t *seq_ids, const int32_t *positions, size_t nq,
+                       const float *rope_cos, const float *rope_sin,
+                       const qvl_attn_dims *dims, void *stream);
+size_t qvl_attention_workspace_bytes(size_t nq, int max_ctx, const qvl_attn_dims *dims);
+int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                         const int32_t *page_table, const int32_t *seq_ids,
+                         const int32_t *positions, size_t nq, int max_ctx, float *out,
+                         const qvl_attn_dims *dims, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+/* ---- greedy decode (tokenizer/src/utils.cpp:34-44) ---------------------
+ * idx[r] = first index of the maximum of logits[r, :n] (strict >, from
+ * -FLT_MAX; NaN never wins; all-NaN/-inf rows give 0). */
+int qvl_argmax_rows(const float *logits, int32_t *idx, size_t rows, size_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QVL_B200_H */

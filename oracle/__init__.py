@@ -1,0 +1,210 @@
+"""Test infrastructure only: ctypes bindings to the CPU checkers.
+
+* ``liboracle.so`` -- the scalar C restatement of the reference's INT8 hot
+  path (oracle.c), built by ``make -C oracle``.
+* ``_ref/libqwen_ref.so`` -- the reference engine's own CPU operators,
+  compiled from its unmodified sources by ``make -C oracle ref`` (only where
+  the reference sources are present; the built file travels with the repo).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
+this module.  The product library never links or calls it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libqwen_ref.so")
+REF_SRC = os.environ.get("QVL_REFERENCE_DIR", "/root/reference")
+
+LANE8_DISPATCH, LANE8, TILED = 0, 1, 2
+
+_P = ctypes.c_void_p
+_Z = ctypes.c_size_t
+_I = ctypes.c_int
+
+
+def build(ref: bool = True) -> None:
+    """Compile the restatement, and the reference library when its sources exist."""
+    subprocess.run(["make", "-C", HERE, "-s", "all"], check=True)
+    if ref and os.path.isdir(REF_SRC):
+        subprocess.run(["make", "-C", HERE, "-s", "-j8", "ref", f"REF={REF_SRC}"], check=True)
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"], "oracle buffers must be C-contiguous"
+    return a.ctypes.data
+
+
+_orc = None
+_ref = None
+
+
+def lib():
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORACLE_SO):
+            build(ref=False)
+        L = ctypes.CDLL(ORACLE_SO)
+        L.orc_quantize_row.argtypes = [_P, _Z, _Z, _P, _P]
+        L.orc_linear_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, _Z, _Z, _I]
+        L.orc_group_sums.argtypes = [_P, _P, _P, _Z, _Z, _Z, _Z]
+        L.orc_swiglu.argtypes = [_P, _P, _Z]
+        L.orc_exp_ref.argtypes = [ctypes.c_float]
+        L.orc_exp_ref.restype = ctypes.c_float
+        L.orc_softmax.argtypes = [_P, _Z]
+        L.orc_rope_inplace.argtypes = [_P, _P, _P, _I, _I]
+        L.orc_attention.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _Z, _I]
+        L.orc_argmax.argtypes = [_P, _Z]
+        L.orc_argmax.restype = _I
+        L.orc_rope_table.argtypes = [_P, _P, _Z, _I, ctypes.c_float]
+        _orc = L
+    return _orc
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        L = ctypes.CDLL(REF_SO)
+        L.ref_i8_kernel.argtypes = [_P, _P, _P, _P, _Z, _Z, _Z, _Z]
+        L.ref_linear_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, _Z, _I, _Z]
+        L.ref_swiglu.argtypes = [_P, _P, _Z]
+        L.ref_softmax.argtypes = [_P, _Z]
+        L.ref_apply_rotary.argtypes = [_P, _P, _P, _Z, _I, _I, _I]
+        L.ref_apply_rotary_cache.argtypes = [_P, _P, _P, _P, _Z, _I, _I, _I, _Z]
+        L.ref_attention.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _Z, _I]
+        _ref = L
+    return _ref
+
+
+# ---------------------------------------------------------------- restatement
+def quantize(x: np.ndarray, g: int):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    q = np.empty((M, K), np.int16)
+    s = np.empty((M, K // g), np.float32)
+    for i in range(M):
+        lib().orc_quantize_row(x[i].ctypes.data, K, g, q[i].ctypes.data, s[i].ctypes.data)
+    return q, s
+
+
+def linear_i8(x, w, ws, g, mode=LANE8_DISPATCH):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), np.float32)
+    lib().orc_linear_i8(_ptr(x), _ptr(w), _ptr(ws), _ptr(y), M, N, K, g, mode)
+    return y
+
+
+def group_sums(q, w, g):
+    M, K = q.shape
+    N = w.shape[0]
+    out = np.empty((M, N, K // g), np.int32)
+    lib().orc_group_sums(_ptr(q), _ptr(w), _ptr(out), M, N, K, g)
+    return out
+
+
+def swiglu(gate, up):
+    g = np.array(gate, dtype=np.float32, copy=True, order="C")
+    u = np.ascontiguousarray(up, dtype=np.float32)
+    lib().orc_swiglu(_ptr(g), _ptr(u), g.size)
+    return g
+
+
+def softmax(x):
+    v = np.array(x, dtype=np.float32, copy=True)
+    lib().orc_softmax(_ptr(v), v.size)
+    return v
+
+
+def exp_ref(x: float) -> float:
+    return lib().orc_exp_ref(x)
+
+
+def rope_inplace(x, cos_row, sin_row):
+    """x: [n_heads, D] fp32, rotated in place (returns x)."""
+    n, D = x.shape
+    lib().orc_rope_inplace(_ptr(x), _ptr(cos_row), _ptr(sin_row), n, D)
+    return x
+
+
+def attention(key_cache, value_cache, q, pos):
+    """key/value_cache: [NKV, S, D] fp32; q: [NH, D] (already rotated)."""
+    NKV, S, D = key_cache.shape
+    NH = q.shape[0]
+    att = np.zeros((NH, S), np.float32)
+    out = np.empty((NH, D), np.float32)
+    lib().orc_attention(_ptr(key_cache), _ptr(value_cache), _ptr(q), _ptr(att), _ptr(out),
+                        NH, NKV, D, S, pos)
+    return out
+
+
+def argmax(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return int(lib().orc_argmax(_ptr(x), x.size))
+
+
+def rope_table(S: int, D: int = 128, theta: float = 5e6):
+    c = np.empty((S, D // 2), np.float32)
+    s = np.empty((S, D // 2), np.float32)
+    lib().orc_rope_table(_ptr(c), _ptr(s), S, D, theta)
+    return c, s
+
+
+# -------------------------------------------------------- compiled reference
+def ref_i8_kernel(x, w, ws, g):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.zeros((M, N), np.float32)
+    ref_lib().ref_i8_kernel(_ptr(x), _ptr(w), _ptr(ws), _ptr(y), M, N, K, g)
+    return y
+
+
+def ref_linear(x, w, ws, group_quantized, g):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.zeros((M, N), np.float32)
+    ref_lib().ref_linear_i8(_ptr(x), _ptr(w), _ptr(ws), _ptr(y), M, N, K, int(group_quantized), g)
+    return y
+
+
+def ref_swiglu(gate, up):
+    g = np.array(gate, dtype=np.float32, copy=True, order="C")
+    u = np.ascontiguousarray(up, dtype=np.float32)
+    ref_lib().ref_swiglu(_ptr(g), _ptr(u), g.size)
+    return g
+
+
+def ref_softmax(x):
+    v = np.array(x, dtype=np.float32, copy=True)
+    ref_lib().ref_softmax(_ptr(v), v.size)
+    return v
+
+
+def ref_rope(x, cos_tab, sin_tab, pos):
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    n, D = x.shape
+    ref_lib().ref_apply_rotary(_ptr(x), _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0], n, D, pos)
+    return x
+
+
+def ref_attention(key_cache, value_cache, q, pos):
+    NKV, S, D = key_cache.shape
+    NH = q.shape[0]
+    att = np.zeros((NH, S), np.float32)
+    out = np.zeros((NH, D), np.float32)
+    ref_lib().ref_attention(_ptr(key_cache), _ptr(value_cache), _ptr(q), _ptr(att), _ptr(out),
+                            NH, NKV, D, S, pos)
+    return out

@@ -1,0 +1,253 @@
+"""Host-side mirror of the reference engine's INT8 hot-path operators, running
+on the sm_100a kernels of ``lib/libqvl_b200.so`` through its C ABI
+(include/qvl_b200.h).
+
+The operator names and argument meanings follow the reference
+(dangtruong-github/qwen3-vl-2b-inference):
+
+=====================  ==========================================================
+this module            reference
+=====================  ==========================================================
+``linear``             ``linear`` INT8 branch, matmul/src/cpu_wrapper.cpp:308-357
+``quantize_rows``      activation prologue, cpu_f32a_i8f32sb_f32c_avx2.cpp:135-177
+``swiglu``             ``swiglu``, layers/src/text_layer.cpp:420-434
+``swiglu_mlp``         gate/up linear + swiglu + down linear, model/src/forward.cpp:621-654
+``rope_kv_append``     ``apply_rotary`` + ``apply_rotary_cache`` + v copy,
+                       layers/src/text_layer.cpp:712-824, model/src/forward.cpp:545-562
+``attention``          ``attn_scores_all_heads`` + ``softmax`` +
+                       ``attn_weighted_sum_all_heads``, layers/src/text_layer.cpp:436-710
+``greedy_decode``      ``greedy_decode``, tokenizer/src/utils.cpp:34-44
+=====================  ==========================================================
+
+Tensors are torch CUDA tensors (torch supplies device memory and streams
+only).  There is no CPU fallback: if the library is missing, importing this
+module raises.  An unsupported combination raises ``QvlError`` (the
+reference prints and calls ``exit(1)``, cpu_wrapper.cpp:394-395).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libqvl_b200.so")
+
+SEM_REFERENCE, SEM_LANE8, SEM_TILED = 0, 1, 2
+DTYPE_FP32, DTYPE_INT32, DTYPE_FP16, DTYPE_INT8, DTYPE_INT4 = 0, 1, 2, 3, 4
+
+EXPORTED = (
+    "qvl_status_string", "qvl_last_cuda_error", "qvl_version", "qvl_quantize_rows",
+    "qvl_linear_i8_workspace_bytes", "qvl_linear_i8", "qvl_linear_q16_i8", "qvl_swiglu",
+    "qvl_swiglu_mlp_workspace_bytes", "qvl_swiglu_mlp_i8", "qvl_rope_kv_append",
+    "qvl_attention_workspace_bytes", "qvl_attention_decode", "qvl_argmax_rows",
+)
+
+
+class QvlError(RuntimeError):
+    pass
+
+
+class AttnDims(ctypes.Structure):
+    _fields_ = [("num_heads", ctypes.c_int), ("num_kv_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("page_size", ctypes.c_int),
+                ("max_pages_per_seq", ctypes.c_int), ("max_pos", ctypes.c_int)]
+
+
+_P, _Z, _I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Load libqvl_b200.so (build it with build.py); raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"libqvl_b200.so not built ({path}); run `python {PKG_DIR}/build.py`")
+    L = ctypes.CDLL(path)
+    L.qvl_status_string.restype = ctypes.c_char_p
+    L.qvl_status_string.argtypes = [_I]
+    L.qvl_version.restype = ctypes.c_char_p
+    L.qvl_quantize_rows.argtypes = [_P, _P, _P, _Z, _Z, _Z, _P]
+    L.qvl_linear_i8_workspace_bytes.restype = _Z
+    L.qvl_linear_i8_workspace_bytes.argtypes = [_Z, _Z, _Z]
+    L.qvl_linear_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, _Z, _I, _Z, _I, _P, _Z, _P]
+    L.qvl_linear_q16_i8.argtypes = [_P, _P, _P, _P, _P, _Z, _Z, _Z, _Z, _I, _P]
+    L.qvl_swiglu.argtypes = [_P, _P, _Z, _P]
+    L.qvl_swiglu_mlp_workspace_bytes.restype = _Z
+    L.qvl_swiglu_mlp_workspace_bytes.argtypes = [_Z, _Z, _Z, _Z]
+    L.qvl_swiglu_mlp_i8.argtypes = [_P] * 8 + [_Z, _Z, _Z, _Z, _I, _P, _Z, _P]
+    L.qvl_rope_kv_append.argtypes = [_P] * 8 + [_Z, _P, _P, ctypes.POINTER(AttnDims), _P]
+    L.qvl_attention_workspace_bytes.restype = _Z
+    L.qvl_attention_workspace_bytes.argtypes = [_Z, _I, ctypes.POINTER(AttnDims)]
+    L.qvl_attention_decode.argtypes = [_P] * 6 + [_Z, _I, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
+    L.qvl_argmax_rows.argtypes = [_P, _P, _Z, _Z, _P]
+    _lib = L
+    return L
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        L = load_library()
+        msg = L.qvl_status_string(rc).decode()
+        cuda = L.qvl_last_cuda_error()
+        raise QvlError(f"{what}: {msg} (status {rc}, last CUDA error {cuda})")
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise QvlError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise QvlError("expected a contiguous tensor")
+    return t.data_ptr()
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class Workspace:
+    """Device scratch owned by the caller and reused across calls (the C ABI
+    never allocates).  Grows on demand outside any timed or captured region."""
+
+    def __init__(self, device=None):
+        self.device = torch.device(device or "cuda")
+        self.buf = torch.empty(0, dtype=torch.uint8, device=self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_default_ws: dict = {}
+
+
+def _ws(ws, device):
+    if ws is not None:
+        return ws
+    key = torch.device(device).index
+    if key not in _default_ws:
+        _default_ws[key] = Workspace(device)
+    return _default_ws[key]
+
+
+# --------------------------------------------------------------------------- ops
+def quantize_rows(x: torch.Tensor, group_size: int, stream=None):
+    """fp32 [M,K] -> (int16 [M,K], fp32 [M,K/g]); the reference's activation prologue."""
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int16, device=x.device)
+    s = torch.empty((M, K // group_size), dtype=torch.float32, device=x.device)
+    _check(load_library().qvl_quantize_rows(_ptr(x), _ptr(q), _ptr(s), M, K, group_size,
+                                            _stream(stream)), "quantize_rows")
+    return q, s
+
+
+def linear(A: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor, C: torch.Tensor | None = None,
+           group_quantized: bool = True, group_size: int = 0, semantics: int = SEM_REFERENCE,
+           workspace: Workspace | None = None, stream=None) -> torch.Tensor:
+    """C[M,N] = A[M,K] (fp32) x dequant(B[N,K] int8, B_scale fp32)^T.
+
+    ``group_quantized=False`` is per-output-row scaling (group size K)."""
+    M, K = A.shape
+    N = B.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    g = group_size if group_quantized else K
+    L = load_library()
+    nbytes = L.qvl_linear_i8_workspace_bytes(M, K, g)
+    ws = _ws(workspace, A.device).get(nbytes)
+    _check(L.qvl_linear_i8(_ptr(A), _ptr(B), _ptr(B_scale), _ptr(C), M, N, K, int(group_quantized),
+                           group_size, semantics, _ptr(ws), ws.numel(), _stream(stream)), "linear")
+    return C
+
+
+def linear_q16(q, q_scales, B, B_scale, group_size, C=None, semantics=SEM_REFERENCE, stream=None):
+    M, K = q.shape
+    N = B.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=q.device)
+    _check(load_library().qvl_linear_q16_i8(_ptr(q), _ptr(q_scales), _ptr(B), _ptr(B_scale), _ptr(C),
+                                            M, N, K, group_size, semantics, _stream(stream)),
+           "linear_q16")
+    return C
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor, stream=None) -> torch.Tensor:
+    """In place: gate = silu(gate) * up."""
+    _check(load_library().qvl_swiglu(_ptr(gate), _ptr(up), gate.numel(), _stream(stream)), "swiglu")
+    return gate
+
+
+def swiglu_mlp(x, w_gate, s_gate, w_up, s_up, w_down, s_down, group_size, out=None,
+               semantics=SEM_REFERENCE, workspace=None, stream=None):
+    """out[M,H] = down(swiglu(gate(x), up(x))) with int8 weights."""
+    M, H = x.shape
+    I = w_gate.shape[0]
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.float32, device=x.device)
+    L = load_library()
+    ws = _ws(workspace, x.device).get(L.qvl_swiglu_mlp_workspace_bytes(M, H, I, group_size))
+    _check(L.qvl_swiglu_mlp_i8(_ptr(x), _ptr(w_gate), _ptr(s_gate), _ptr(w_up), _ptr(s_up),
+                               _ptr(w_down), _ptr(s_down), _ptr(out), M, H, I, group_size, semantics,
+                               _ptr(ws), ws.numel(), _stream(stream)), "swiglu_mlp")
+    return out
+
+
+class PagedKV:
+    """One layer's FP16 KV pages [num_pages, NKV, page_size, D] plus a page table
+    [num_seqs, max_pages_per_seq] (identity-mapped unless given)."""
+
+    def __init__(self, num_seqs, max_ctx, num_heads=16, num_kv_heads=8, head_dim=128,
+                 page_size=64, max_pos=None, device="cuda", page_table=None):
+        self.page_size = page_size
+        self.maxp = (max_ctx + page_size - 1) // page_size
+        num_pages = num_seqs * self.maxp
+        shape = (num_pages, num_kv_heads, page_size, head_dim)
+        self.k = torch.zeros(shape, dtype=torch.float16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.float16, device=device)
+        if page_table is None:
+            page_table = torch.arange(num_pages, dtype=torch.int32, device=device).view(num_seqs, self.maxp)
+        self.page_table = page_table.contiguous()
+        self.dims = AttnDims(num_heads, num_kv_heads, head_dim, page_size, self.maxp,
+                             max_pos if max_pos is not None else max_ctx)
+
+
+def rope_kv_append(q, k_new, v_new, kv: PagedKV, seq_ids, positions, rope_cos, rope_sin, stream=None):
+    """Rotate q in place; rotate k_new and write k/v (fp16) at each query's position."""
+    nq = q.shape[0]
+    _check(load_library().qvl_rope_kv_append(
+        _ptr(q), _ptr(k_new), _ptr(v_new), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table),
+        _ptr(seq_ids), _ptr(positions), nq, _ptr(rope_cos), _ptr(rope_sin), ctypes.byref(kv.dims),
+        _stream(stream)), "rope_kv_append")
+    return q
+
+
+def attention(q, kv: PagedKV, seq_ids, positions, max_ctx, out=None, workspace=None, stream=None):
+    """out[nq, NH, D] = softmax(q k^T / sqrt(D)) v over positions [0, pos] of each query."""
+    nq = q.shape[0]
+    if out is None:
+        out = torch.empty_like(q)
+    L = load_library()
+    ws = _ws(workspace, q.device).get(L.qvl_attention_workspace_bytes(nq, max_ctx, ctypes.byref(kv.dims)))
+    _check(L.qvl_attention_decode(_ptr(q), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table),
+                                  _ptr(seq_ids), _ptr(positions), nq, max_ctx, _ptr(out),
+                                  ctypes.byref(kv.dims), _ptr(ws), ws.numel(), _stream(stream)),
+           "attention")
+    return out
+
+
+def greedy_decode(logits: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    """int32 [rows]: first index of the row maximum."""
+    rows = logits.shape[0] if logits.dim() == 2 else 1
+    n = logits.shape[-1]
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _check(load_library().qvl_argmax_rows(_ptr(logits), _ptr(out), rows, n, _stream(stream)),
+           "greedy_decode")
+    return out

@@ -1,0 +1,244 @@
+// extern "C" entry points declared in include/qvl_b200.h: argument checks,
+// workspace carving and kernel sequencing.  No entry point allocates memory,
+// synchronises the stream, exits or traps.
+#include <cstdio>
+#include <cstring>
+#include "common.cuh"
+#include "qact.cuh"
+#include "gemv_i8.cuh"
+#include "gemm_i8_tc.cuh"
+#include "swiglu.cuh"
+#include "attention.cuh"
+#include "argmax.cuh"
+
+namespace {
+int g_last_cuda_error = 0;
+
+inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+size_t qbuf_bytes(size_t M, size_t K, size_t g) {
+    return align256(M * K * sizeof(int16_t)) + align256(M * (K / g) * sizeof(float));
+}
+
+// Largest row tile (<= 8) whose int16 activations fit in shared memory.
+int gemv_rows_per_launch(size_t K, size_t g) {
+    for (int mr = 8; mr >= 1; mr >>= 1)
+        if (qvl::gemv_smem_bytes(mr, (int)K, (int)g) <= 200 * 1024) return mr;
+    return 0;
+}
+
+bool lane8_for(int semantics, size_t M, size_t N, size_t K) {
+    if (semantics == QVL_SEM_LANE8) return true;
+    if (semantics == QVL_SEM_TILED) return false;
+    return M == 1 && N >= 1024 && K >= 1024;   // cpu_f32a_i8f32sb_f32c_avx2.cpp:464
+}
+
+// y[M,N] from pre-quantised activations: CUDA-core GEMV for small M (and for
+// the LANE8 summation order at any M), tensor cores for TILED at M >= 16.
+int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const float *Bs, float *C,
+                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st) {
+    if (!lane8 && qvl::gemm_tc_supported(M, N, K, g)) {
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, B, Bs, C, (int)M, (int)N, (int)K, (int)g, st));
+        return QVL_OK;
+    }
+    const int mr = gemv_rows_per_launch(K, g);
+    if (mr == 0) return QVL_ERR_UNSUPPORTED;
+    const size_t G = K / g;
+    for (size_t m0 = 0; m0 < M; m0 += mr) {
+        qvl::GemvArgs a;
+        a.q = q + m0 * K;
+        a.qs = qs + m0 * G;
+        a.W = B;
+        a.ws = Bs;
+        a.y = C + m0 * N;
+        a.M = (int)((M - m0) < (size_t)mr ? (M - m0) : (size_t)mr);
+        a.N = (int)N;
+        a.K = (int)K;
+        a.g = (int)g;
+        a.ldy = (long)N;
+        QVL_CUDA_TRY(qvl::launch_gemv_i8(a, lane8, st));
+    }
+    return QVL_OK;
+}
+
+int check_linear_shape(size_t M, size_t N, size_t K, size_t g) {
+    if (M == 0 || N == 0 || K == 0) return QVL_ERR_INVALID;
+    if (K > (1u << 30) || N > (1u << 30) || M > (1u << 20)) return QVL_ERR_INVALID;
+    if (!qvl::gemv_shape_supported((int)K, (int)g)) return QVL_ERR_UNSUPPORTED;
+    return QVL_OK;
+}
+}  // namespace
+
+extern "C" void qvl_internal_set_cuda_error(int err) { g_last_cuda_error = err; }
+
+extern "C" {
+
+const char *qvl_status_string(int s) {
+    switch (s) {
+        case QVL_OK: return "ok";
+        case QVL_ERR_INVALID: return "invalid argument";
+        case QVL_ERR_UNSUPPORTED: return "unsupported shape or dtype combination";
+        case QVL_ERR_CUDA: return "CUDA runtime error";
+        case QVL_ERR_WORKSPACE: return "workspace missing or too small";
+    }
+    return "unknown status";
+}
+
+int qvl_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char *qvl_version(void) { return "qvl_b200 0.1"; }
+
+int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, size_t K,
+                      size_t group_size, void *stream) {
+    if (!x || !q || !q_scales) return QVL_ERR_INVALID;
+    if (M == 0 || K == 0 || group_size == 0 || K % group_size || group_size % 16) return QVL_ERR_INVALID;
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, q, q_scales, (int)M, (int)K, (int)group_size,
+                                           (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+size_t qvl_linear_i8_workspace_bytes(size_t M, size_t K, size_t group_size) {
+    if (group_size == 0 || K % group_size) return 0;
+    return qbuf_bytes(M, K, group_size);
+}
+
+int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
+                      const float *B_scales, float *C, size_t M, size_t N, size_t K,
+                      size_t group_size, int semantics, void *stream) {
+    if (!q || !q_scales || !B || !B_scales || !C) return QVL_ERR_INVALID;
+    int rc = check_linear_shape(M, N, K, group_size);
+    if (rc) return rc;
+    if (!aligned(q, 16) || !aligned(B, 16) || (K * sizeof(int8_t)) % 16) return QVL_ERR_INVALID;
+    if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    return run_q16_linear(q, q_scales, B, B_scales, C, M, N, K, group_size,
+                          lane8_for(semantics, M, N, K), (cudaStream_t)stream);
+}
+
+int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float *C, size_t M,
+                  size_t N, size_t K, int group_quantized, size_t group_size, int semantics,
+                  void *workspace, size_t workspace_bytes, void *stream) {
+    if (!A || !B || !B_scales || !C) return QVL_ERR_INVALID;
+    const size_t g = group_quantized ? group_size : K;
+    int rc = check_linear_shape(M, N, K, g);
+    if (rc) return rc;
+    if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    const size_t need = qbuf_bytes(M, K, g);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    if (!aligned(B, 16)) return QVL_ERR_INVALID;
+    int16_t *q = static_cast<int16_t *>(workspace);
+    float *qs = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * K * 2));
+    cudaStream_t st = (cudaStream_t)stream;
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
+    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st);
+}
+
+int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
+    if (!gate || !up) return QVL_ERR_INVALID;
+    if (n == 0) return QVL_OK;
+    QVL_CUDA_TRY(qvl::launch_swiglu(gate, up, (long)n, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+size_t qvl_swiglu_mlp_workspace_bytes(size_t M, size_t H, size_t I, size_t g) {
+    if (g == 0 || H % g || I % g) return 0;
+    return qbuf_bytes(M, H, g) + 2 * align256(M * I * sizeof(float)) + qbuf_bytes(M, I, g);
+}
+
+int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const int8_t *Wu,
+                      const float *su, const int8_t *Wd, const float *sd, float *out, size_t M,
+                      size_t H, size_t I, size_t group_size, int semantics, void *workspace,
+                      size_t workspace_bytes, void *stream) {
+    if (!x || !Wg || !sg || !Wu || !su || !Wd || !sd || !out) return QVL_ERR_INVALID;
+    int rc = check_linear_shape(M, I, H, group_size);
+    if (!rc) rc = check_linear_shape(M, H, I, group_size);
+    if (rc) return rc;
+    if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    const size_t need = qvl_swiglu_mlp_workspace_bytes(M, H, I, group_size);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    char *w = static_cast<char *>(workspace);
+    int16_t *qx = reinterpret_cast<int16_t *>(w);
+    float *qxs = reinterpret_cast<float *>(w + align256(M * H * 2));
+    w += qbuf_bytes(M, H, group_size);
+    float *gate = reinterpret_cast<float *>(w);
+    w += align256(M * I * 4);
+    float *up = reinterpret_cast<float *>(w);
+    w += align256(M * I * 4);
+    int16_t *qh = reinterpret_cast<int16_t *>(w);
+    float *qhs = reinterpret_cast<float *>(w + align256(M * I * 2));
+    cudaStream_t st = (cudaStream_t)stream;
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)group_size, st));
+    const bool l_gu = lane8_for(semantics, M, I, H);
+    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, group_size, l_gu, st);
+    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, group_size, l_gu, st);
+    if (rc) return rc;
+    QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)group_size, st));
+    return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, group_size,
+                          lane8_for(semantics, M, H, I), st);
+}
+
+static int check_attn_dims(const qvl_attn_dims *d) {
+    if (!d) return QVL_ERR_INVALID;
+    if (d->head_dim != 128) return QVL_ERR_UNSUPPORTED;
+    if (d->num_heads <= 0 || d->num_kv_heads <= 0 || d->num_heads % d->num_kv_heads) return QVL_ERR_INVALID;
+    const int kvm = d->num_heads / d->num_kv_heads;
+    if (kvm != 1 && kvm != 2 && kvm != 4) return QVL_ERR_UNSUPPORTED;
+    if (d->page_size <= 0 || d->max_pages_per_seq <= 0 || d->max_pos <= 0) return QVL_ERR_INVALID;
+    return QVL_OK;
+}
+
+int qvl_rope_kv_append(float *q, const float *k_new, const float *v_new, uint16_t *k_pages,
+                       uint16_t *v_pages, const int32_t *page_table, const int32_t *seq_ids,
+                       const int32_t *positions, size_t nq, const float *rope_cos,
+                       const float *rope_sin, const qvl_attn_dims *dims, void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !positions || !rope_cos || !rope_sin) return QVL_ERR_INVALID;
+    if (k_new && (!v_new || !k_pages || !v_pages || !page_table || !seq_ids)) return QVL_ERR_INVALID;
+    if (nq == 0) return QVL_OK;
+    qvl::RopeArgs a;
+    a.q = q; a.k_new = k_new; a.v_new = v_new; a.k_pages = k_pages; a.v_pages = v_pages;
+    a.page_table = page_table; a.seq_ids = seq_ids; a.positions = positions; a.nq = nq;
+    a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    QVL_CUDA_TRY(qvl::launch_rope_append(a, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+size_t qvl_attention_workspace_bytes(size_t nq, int max_ctx, const qvl_attn_dims *dims) {
+    if (check_attn_dims(dims) || max_ctx <= 0 || nq == 0) return 0;
+    return qvl::attn_scratch_layout(nq, max_ctx, dims->num_heads, dims->num_kv_heads).total;
+}
+
+int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                         const int32_t *page_table, const int32_t *seq_ids,
+                         const int32_t *positions, size_t nq, int max_ctx, float *out,
+                         const qvl_attn_dims *dims, void *workspace, size_t workspace_bytes,
+                         void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !k_pages || !v_pages || !page_table || !seq_ids || !positions || !out) return QVL_ERR_INVALID;
+    if (max_ctx <= 0) return QVL_ERR_INVALID;
+    if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(q, 16)) return QVL_ERR_INVALID;
+    if (nq == 0) return QVL_OK;
+    const size_t need = qvl_attention_workspace_bytes(nq, max_ctx, dims);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    qvl::AttnArgs a;
+    a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
+    a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    QVL_CUDA_TRY(qvl::launch_attention(a, workspace, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_argmax_rows(const float *logits, int32_t *idx, size_t rows, size_t n, void *stream) {
+    if (!logits || !idx || n == 0 || n > (size_t)INT32_MAX) return QVL_ERR_INVALID;
+    if (rows == 0) return QVL_OK;
+    QVL_CUDA_TRY(qvl::launch_argmax_rows(logits, idx, (long)rows, (long)n, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+}  // extern "C"

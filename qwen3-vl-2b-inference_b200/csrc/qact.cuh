@@ -1,0 +1,54 @@
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "common.cuh"
+
+namespace qvl {
+cudaError_t launch_quantize_rows(const float *x, int16_t *q, float *s, int M, int K, int g,
+                                 cudaStream_t stream);
+
+__device__ __forceinline__ float inv127() { return __int_as_float(0x3c010204); }  // (float)1/127
+
+// Sum of squares of one group in the reference order; valid in lane t16 == 0
+// of the half-warp, broadcast to all 16.
+__device__ __forceinline__ float group_sumsq_ref(const float *xg, int g, int t16) {
+    float acc = 0.0f;
+    for (int j = 0; j < g; j += 16) {
+        float v = xg[j + t16];
+        acc = fma_rn(v, v, acc);
+    }
+    const unsigned full = 0xffffffffu;
+    float o = __shfl_down_sync(full, acc, 8, 16);
+    float v = add_rn(acc, o);                     // lane l<8: v_l = a0_l + a1_l
+    o = __shfl_down_sync(full, v, 4, 16);
+    float u = add_rn(v, o);                       // l<4: u_l = v_l + v_{l+4}
+    o = __shfl_down_sync(full, u, 1, 16);
+    float p = add_rn(u, o);                       // l=0: u0+u1 ; l=2: u2+u3
+    o = __shfl_down_sync(full, p, 2, 16);
+    float r = add_rn(p, o);                       // l=0: (u0+u1)+(u2+u3)
+    return __shfl_sync(full, r, 0, 16);
+}
+
+__device__ __forceinline__ int16_t quant_one(float x, float inv) {
+    float p = mul_rn(x, inv);
+    int r;
+    if (!(p > -2147483648.0f && p < 2147483648.0f)) r = INT32_MIN;  // cvtps_epi32 overflow/NaN
+    else r = __float2int_rn(p);
+    r = max(-32768, min(32767, r));                                  // packs_epi32
+    return (int16_t)r;
+}
+
+// Quantise group `gi` of row x (length g) into q/s; called by one half-warp.
+__device__ __forceinline__ void quantize_group(const float *xg, int16_t *qg, float *sg,
+                                               int g, int t16, bool write = true) {
+    float ss = group_sumsq_ref(xg, g, t16);
+    float inv_g = __fdiv_rn(1.0f, (float)g);
+    float rms = __fsqrt_rn(fma_rn(ss, inv_g, 1e-6f));
+    float s = mul_rn(rms, inv127());
+    if (write && t16 == 0) *sg = s;
+    float inv = __fdiv_rn(1.0f, s);
+    if (write)
+        for (int j = t16; j < g; j += 16) qg[j] = quant_one(xg[j], inv);
+}
+
+}  // namespace qvl
