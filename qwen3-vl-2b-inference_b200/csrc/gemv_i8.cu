@@ -298,6 +298,173 @@ gemv_i8_kernel(const int16_t *__restrict q, const float *__restrict qs,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fast path: M <= 4 rows, g >= 128 (segments of >= 8 lanes), K <= 12*512,
+// K/g <= 64.  Every lane issues all IT 16-byte loads of its warp's row at
+// once (one 512-byte step per load), plus the row's weight scales, before
+// touching any of them, so a single wave of warps keeps the decode-shape
+// matrices in flight.  Rows are walked with pointer increments only; when
+// IT <= 4 the next row's loads are issued before the current row is reduced.
+template <int MR, bool LANE, int IT>
+__global__ void __launch_bounds__(kThreads)
+gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
+                    const int8_t *__restrict W, const float *__restrict ws, float *__restrict y,
+                    int M, int N, int K, int g, long ldy, int seglog) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    int16_t *q_s = reinterpret_cast<int16_t *>(smem);
+    const int G = K / g;
+    float *qs_s = reinterpret_cast<float *>(smem + (size_t)MR * K * sizeof(int16_t));
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nwarps = gridDim.x * kWarpsPerBlock;
+    const int NCH = K / 16;
+    const int seg = 1 << seglog;
+    const int IPG = (seg == 32) ? (g >> 9) : 1;   // steps per group (g >= 512)
+    const int GPI = 32 >> seglog;                  // groups per step (g < 512)
+    constexpr bool kDouble = IT <= 4;
+
+    int n = blockIdx.x * kWarpsPerBlock + warp;
+    uint4 wr[IT];
+    float wsr[2];
+    auto issue = [&](int row, uint4 *dst, float *sdst) {
+        const uint4 *base = reinterpret_cast<const uint4 *>(W + (long)row * K) + lane;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int c = it * 32 + lane;
+            dst[it] = (c < NCH) ? ld_stream_v4(base + it * 32) : make_uint4(0, 0, 0, 0);
+        }
+        const float *wsrow = ws + (long)row * G;
+        sdst[0] = (lane < G) ? __ldg(wsrow + lane) : 0.0f;
+        sdst[1] = (lane + 32 < G) ? __ldg(wsrow + lane + 32) : 0.0f;
+    };
+    if (n < N) issue(n, wr, wsr);
+
+    pdl_launch_dependents();
+    pdl_wait();
+    {
+        const int nq16 = M * K / 8;
+        const int4 *src = reinterpret_cast<const int4 *>(q);
+        int4 *dst = reinterpret_cast<int4 *>(q_s);
+        for (int i = threadIdx.x; i < nq16; i += kThreads) dst[i] = src[i];
+        for (int i = threadIdx.x; i < M * G; i += kThreads) qs_s[i] = qs[i];
+    }
+    __syncthreads();
+
+    const unsigned full = 0xffffffffu;
+    const int pos = lane & (seg - 1);
+    const int d1 = seg >> 1, d2 = seg >> 2, d3 = seg >> 3;   // transposing-butterfly distances
+
+    for (; n < N; n += nwarps) {
+        uint4 nx[kDouble ? IT : 1];
+        float nws[2] = {0.0f, 0.0f};
+        const int nn = n + nwarps;
+        if constexpr (kDouble) {
+            if (nn < N) issue(nn, nx, nws);
+        }
+        float cf[MR];
+        int part[MR][8];
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            cf[m] = 0.0f;
+#pragma unroll
+            for (int l = 0; l < 8; ++l) part[m][l] = 0;
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            if (it * 32 >= NCH) break;
+            const int c = it * 32 + lane;
+            const int cc = (c < NCH) ? c : 0;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                if (m < M) {
+                    const int4 *ap = reinterpret_cast<const int4 *>(q_s + (size_t)m * K + cc * 16);
+                    madd_chunk(wr[it], ap[0], ap[1], part[m]);
+                }
+            }
+            const bool group_end = (seg == 32) ? ((it + 1) % IPG == 0) : true;
+            if (!group_end) continue;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                if (m >= M) continue;
+                if constexpr (LANE) {
+                    int v[8];
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) v[l] = part[m][l];
+                    bool up = lane & d1;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        int send = up ? v[i] : v[i + 4];
+                        int keep = up ? v[i + 4] : v[i];
+                        v[i] = keep + __shfl_xor_sync(full, send, d1);
+                    }
+                    up = lane & d2;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        int send = up ? v[i] : v[i + 2];
+                        int keep = up ? v[i + 2] : v[i];
+                        v[i] = keep + __shfl_xor_sync(full, send, d2);
+                    }
+                    up = lane & d3;
+                    int r = (up ? v[1] : v[0]) + __shfl_xor_sync(full, up ? v[0] : v[1], d3);
+                    for (int d = seg >> 4; d >= 1; d >>= 1) r += __shfl_xor_sync(full, r, d);
+                    if (seg == 32) {
+                        const int gi = it / IPG;
+                        const float wsv = __shfl_sync(full, (gi >> 5) ? wsr[1] : wsr[0], gi & 31);
+                        cf[m] = fma_rn(__int2float_rn(r), mul_rn(qs_s[m * G + gi], wsv), cf[m]);
+                    } else {
+                        for (int sgi = 0; sgi < GPI; ++sgi) {
+                            const int vs = __shfl_sync(full, r, sgi * seg + pos);
+                            const int gi = it * GPI + sgi;
+                            const float wsv = __shfl_sync(full, ((gi >> 5) & 1) ? wsr[1] : wsr[0], gi & 31);
+                            if (gi < G) cf[m] = fma_rn(__int2float_rn(vs), mul_rn(qs_s[m * G + gi], wsv), cf[m]);
+                        }
+                    }
+                } else {
+                    int t = 0;
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) t += part[m][l];
+                    for (int d = seg >> 1; d >= 1; d >>= 1) t += __shfl_xor_sync(full, t, d);
+                    if (seg == 32) {
+                        const int gi = it / IPG;
+                        const float wsv = __shfl_sync(full, (gi >> 5) ? wsr[1] : wsr[0], gi & 31);
+                        cf[m] = fma_rn(mul_rn(__int2float_rn(t), qs_s[m * G + gi]), wsv, cf[m]);
+                    } else {
+                        for (int sgi = 0; sgi < GPI; ++sgi) {
+                            const int ts = __shfl_sync(full, t, sgi * seg);
+                            const int gi = it * GPI + sgi;
+                            const float wsv = __shfl_sync(full, ((gi >> 5) & 1) ? wsr[1] : wsr[0], gi & 31);
+                            if (gi < G) cf[m] = fma_rn(mul_rn(__int2float_rn(ts), qs_s[m * G + gi]), wsv, cf[m]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int l = 0; l < 8; ++l) part[m][l] = 0;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            if (m >= M) continue;
+            float out = cf[m];
+            if constexpr (LANE) {
+                // (l, l+4) pairs, then (u0+u1) + (u2+u3): partners at d1, d3, d2
+                float u = add_rn(out, __shfl_xor_sync(full, out, d1));
+                float p = add_rn(u, __shfl_xor_sync(full, u, d3));
+                out = add_rn(p, __shfl_xor_sync(full, p, d2));
+            }
+            if (lane == 0) y[(long)m * ldy + n] = out;
+        }
+        if constexpr (kDouble) {
+#pragma unroll
+            for (int it = 0; it < IT; ++it) wr[it] = nx[it];
+            wsr[0] = nws[0];
+            wsr[1] = nws[1];
+        } else {
+            if (nn < N) issue(nn, wr, wsr);
+        }
+    }
+}
+
 namespace {
 
 template <int MR, bool LANE, int SEGLOG>
@@ -365,8 +532,67 @@ size_t gemv_smem_bytes(int M, int K, int g) {
     return (size_t)MR * K * 2 + (size_t)MR * (K / g) * 4;
 }
 
+namespace {
+template <int MR, bool LANE, int IT>
+cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
+    const int G = a.K / a.g;
+    size_t smem = (size_t)MR * a.K * sizeof(int16_t) + (size_t)MR * G * sizeof(float);
+    auto kern = gemv_i8_fast_kernel<MR, LANE, IT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    int dev = 0, sms = 148, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    if (per_sm < 1) per_sm = 1;
+    long want = (a.N + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    long cap = (long)sms * per_sm;
+    int grid = (int)(want < cap ? want : cap);
+    const int cpg = a.g / 16;
+    int seglog = 0;
+    while ((1 << seglog) < (cpg < 32 ? cpg : 32)) ++seglog;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy, seglog);
+}
+
+template <int MR, bool LANE>
+cudaError_t launch_fast_it(const GemvArgs &a, cudaStream_t s) {
+    const int it = (a.K + 511) / 512;
+    if (it <= 1) return launch_fast_t<MR, LANE, 1>(a, s);
+    if (it <= 2) return launch_fast_t<MR, LANE, 2>(a, s);
+    if (it <= 4) return launch_fast_t<MR, LANE, 4>(a, s);
+    if (it <= 8) return launch_fast_t<MR, LANE, 8>(a, s);
+    return launch_fast_t<MR, LANE, 12>(a, s);
+}
+
+template <bool LANE>
+cudaError_t launch_fast_mr(const GemvArgs &a, cudaStream_t s) {
+    if (a.M <= 1) return launch_fast_it<1, LANE>(a, s);
+    if (a.M <= 2) return launch_fast_it<2, LANE>(a, s);
+    return launch_fast_it<4, LANE>(a, s);
+}
+}  // namespace
+
+bool gemv_fast_eligible(int M, int K, int g) {
+    return M <= 4 && g >= 128 && K <= 12 * 512 && (K / g) <= 64 && gemv_shape_supported(K, g);
+}
+
 cudaError_t launch_gemv_i8(const GemvArgs &a, bool lane8, cudaStream_t stream) {
+    if (gemv_fast_eligible(a.M, a.K, a.g))
+        return lane8 ? launch_fast_mr<true>(a, stream) : launch_fast_mr<false>(a, stream);
     return lane8 ? launch_mr<true>(a, stream) : launch_mr<false>(a, stream);
 }
+
 
 }  // namespace qvl
