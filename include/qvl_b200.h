@@ -143,6 +143,33 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
                          const qvl_attn_dims *dims, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* ---- attention without a caller workspace -----------------------------
+ * No counterpart in the reference.  Same inputs, outputs and result as
+ * qvl_attention_decode, but the split-K scratch lives in a fixed device array
+ * compiled into this library instead of a caller-provided workspace.  It is
+ * for hosts that cannot allocate device memory when they call in: a plugin
+ * running inside a framework that owns all device memory through its own
+ * allocator, or a caller that must not allocate on its serving path.
+ * Limits and rules:
+ *   - The scratch is QVL_ATTN_STATIC_SCRATCH_BYTES per GPU that loads this
+ *     library, held until process exit.  A call that needs more
+ *     (qvl_attention_workspace_bytes(nq, max_ctx, dims) larger than that)
+ *     returns QVL_ERR_WORKSPACE and launches nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress with that device current); make that first call
+ *     before any stream capture on the device.
+ *   - Every call on a device shares the one array, so calls whose kernels may
+ *     overlap on the GPU (different streams without ordering) race; order
+ *     them on one stream.  No scratch entry is read before the same call
+ *     writes it, so nothing needs clearing between calls.
+ *   - Calls no allocator (no cudaMalloc/cudaFree). */
+#define QVL_ATTN_STATIC_SCRATCH_BYTES (32u << 20)
+int qvl_attention_decode_static(const float *q, const uint16_t *k_pages,
+                                const uint16_t *v_pages, const int32_t *page_table,
+                                const int32_t *seq_ids, const int32_t *positions, size_t nq,
+                                int max_ctx, float *out, const qvl_attn_dims *dims,
+                                void *stream);
+
 /* ---- greedy decode (tokenizer/src/utils.cpp:34-44) ---------------------
  * idx[r] = first index of the maximum of logits[r, :n] (strict >, from
  * -FLT_MAX; NaN never wins; all-NaN/-inf rows give 0). */
