@@ -93,6 +93,7 @@ const char *qvl_version(void) { return "qvl_b200 0.1"; }
 int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, size_t K,
                       size_t group_size, void *stream) {
     if (!x || !q || !q_scales) return QVL_ERR_INVALID;
+    if (!aligned(x, 16)) return QVL_ERR_INVALID;
     if (M == 0 || K == 0 || group_size == 0 || K % group_size || group_size % 16) return QVL_ERR_INVALID;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(x, q, q_scales, (int)M, (int)K, (int)group_size,
                                            (cudaStream_t)stream));
@@ -126,7 +127,7 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
     const size_t need = qbuf_bytes(M, K, g);
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
-    if (!aligned(B, 16)) return QVL_ERR_INVALID;
+    if (!aligned(B, 16) || !aligned(A, 16)) return QVL_ERR_INVALID;
     int16_t *q = static_cast<int16_t *>(workspace);
     float *qs = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * K * 2));
     cudaStream_t st = (cudaStream_t)stream;
@@ -151,6 +152,7 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
                       size_t H, size_t I, size_t group_size, int semantics, void *workspace,
                       size_t workspace_bytes, void *stream) {
     if (!x || !Wg || !sg || !Wu || !su || !Wd || !sd || !out) return QVL_ERR_INVALID;
+    if (!aligned(x, 16)) return QVL_ERR_INVALID;
     int rc = check_linear_shape(M, I, H, group_size);
     if (!rc) rc = check_linear_shape(M, H, I, group_size);
     if (rc) return rc;

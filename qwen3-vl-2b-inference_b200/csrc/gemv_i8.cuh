@@ -16,6 +16,7 @@ struct GemvArgs {
 };
 
 bool gemv_shape_supported(int K, int g);
+bool gemv_fast_eligible(int M, int K, int g);
 size_t gemv_smem_bytes(int M, int K, int g);
 // M <= 8 rows; lane8 selects the M=1 decode summation order.
 cudaError_t launch_gemv_i8(const GemvArgs &a, bool lane8, cudaStream_t stream);

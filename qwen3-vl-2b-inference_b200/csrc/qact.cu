@@ -12,34 +12,61 @@
 
 namespace qvl {
 
-// grid: (ceil(G / 8), M); block: 128 threads = 8 half-warps, one group each.
-__global__ void __launch_bounds__(128) quantize_rows_kernel(const float *__restrict x,
+// grid: (ceil(G / gpb), M); block 256; gpb = groups per block (<= 16, at
+// most 8192 values).  The block's slice of x is staged in shared memory, then
+// each half-warp computes the scale of one group (the reference's sequential
+// fused chain cannot be split) and all 256 threads quantise the slice.
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float *__restrict x,
                                                             int16_t *__restrict q,
-                                                            float *__restrict s, int K, int g) {
+                                                            float *__restrict s, int K, int g,
+                                                            int gpb) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float inv_s[16];
     pdl_launch_dependents();
     pdl_wait();
     const int G = K / g;
-    int gi = blockIdx.x * 8 + (threadIdx.x >> 4);
+    const int g0 = blockIdx.x * gpb;
+    const int ng = min(gpb, G - g0);
     const int row = blockIdx.y;
-    const bool active = gi < G;   // whole half-warps only: keep them in the shuffles
-    if (!active) gi = G - 1;
-    const size_t off = (size_t)row * K + (size_t)gi * g;
-    quantize_group(x + off, q + off, s + (size_t)row * G + gi, g, threadIdx.x & 15, active);
+    const size_t base = (size_t)row * K + (size_t)g0 * g;
+    const int n = ng * g;
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(x + base)[i];
+    __syncthreads();
+    const int hw = threadIdx.x >> 4;
+    const bool active = hw < ng;        // whole half-warps only: keep them in the shuffles
+    const int gl = active ? hw : 0;
+    const float sc = group_scale_ref(xs + (size_t)gl * g, g, threadIdx.x & 15);
+    if (active && (threadIdx.x & 15) == 0) {
+        s[(size_t)row * G + g0 + gl] = sc;
+        inv_s[gl] = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) q[base + i] = quant_one(xs[i], inv_s[i / g]);
 }
 
 cudaError_t launch_quantize_rows(const float *x, int16_t *q, float *s, int M, int K, int g,
                                  cudaStream_t stream) {
     const int G = K / g;
+    int gpb = 8192 / g;
+    gpb = gpb < 1 ? 1 : (gpb > 16 ? 16 : gpb);
+    const size_t smem = (size_t)gpb * g * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(quantize_rows_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((G + 7) / 8, M);
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3((G + gpb - 1) / gpb, M);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, q, s, K, g);
+    return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, q, s, K, g, gpb);
 }
 
 }  // namespace qvl

@@ -13,6 +13,7 @@ __device__ __forceinline__ float inv127() { return __int_as_float(0x3c010204); }
 // of the half-warp, broadcast to all 16.
 __device__ __forceinline__ float group_sumsq_ref(const float *xg, int g, int t16) {
     float acc = 0.0f;
+#pragma unroll 16
     for (int j = 0; j < g; j += 16) {
         float v = xg[j + t16];
         acc = fma_rn(v, v, acc);
@@ -49,6 +50,15 @@ __device__ __forceinline__ void quantize_group(const float *xg, int16_t *qg, flo
     float inv = __fdiv_rn(1.0f, s);
     if (write)
         for (int j = t16; j < g; j += 16) qg[j] = quant_one(xg[j], inv);
+}
+
+
+// Scale of one group: s = sqrtf(sum(x^2) * (1/g) + 1e-6) * (1/127), the sum in
+// the reference order (group_sumsq_ref).  Called by a whole half-warp.
+__device__ __forceinline__ float group_scale_ref(const float *xg, int g, int t16) {
+    float ss = group_sumsq_ref(xg, g, t16);
+    float inv_g = __fdiv_rn(1.0f, (float)g);
+    return mul_rn(__fsqrt_rn(fma_rn(ss, inv_g, 1e-6f)), inv127());
 }
 
 }  // namespace qvl
