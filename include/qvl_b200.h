@@ -54,6 +54,10 @@ extern "C" {
  *       Use this for a batch of independent decode requests.
  *   QVL_SEM_TILED: the M>1 kernel (:538-653): per group the whole int32 sum
  *       is converted and accumulated as fma(float(S) * a_s, w_s, acc). */
+/* OR-ed into `semantics`: add the product into C (C += A.B^T) instead of
+ * overwriting it -- the residual add_vector after o_proj/down_proj
+ * (model/src/forward.cpp:604, :661), same rounding as a separate add. */
+#define QVL_SEM_ACCUMULATE 0x100
 #define QVL_SEM_REFERENCE 0
 #define QVL_SEM_LANE8 1
 #define QVL_SEM_TILED 2
@@ -93,6 +97,12 @@ int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
 /* ---- SwiGLU (layers/src/text_layer.cpp:420-434) ------------------------
  * gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i], in place, n elements. */
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);
+
+/* swiglu followed by the down projection's activation quantisation, without
+ * materialising the fp32 SwiGLU output: q/q_scales = quantize_rows(
+ * swiglu(gate, up)) for M rows of I values (gate/up are not modified). */
+int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, float *q_scales,
+                             size_t M, size_t I, size_t group_size, void *stream);
 
 /* Fused MLP chain: out[M,H] = down(swiglu(gate(x), up(x))), the sequence of
  * model/src/forward.cpp:621-654 (gate/up linear, swiglu, down linear).
@@ -142,6 +152,33 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
                          const int32_t *positions, size_t nq, int max_ctx, float *out,
                          const qvl_attn_dims *dims, void *workspace,
                          size_t workspace_bytes, void *stream);
+
+/* QK-norm + RoPE + KV append in one launch: rms_norm_inplace of every q and
+ * k head with the layer's INT8 q_norm / k_norm weights (model/src/forward.cpp:
+ * 531-538; layers/src/text_layer.cpp:234-272), then qvl_rope_kv_append.
+ * q_norm_w/k_norm_w int8 [D], *_s fp32 [D / norm_group]. */
+int qvl_qknorm_rope_kv_append(float *q, const float *k_new, const float *v_new, uint16_t *k_pages,
+                              uint16_t *v_pages, const int32_t *page_table, const int32_t *seq_ids,
+                              const int32_t *positions, size_t nq, const float *rope_cos,
+                              const float *rope_sin, const int8_t *q_norm_w, const float *q_norm_s,
+                              const int8_t *k_norm_w, const float *k_norm_s, size_t norm_group,
+                              float eps, const qvl_attn_dims *dims, void *stream);
+
+/* ---- RMSNorm and embedding (layers/src/text_layer.cpp:3-300) ------------
+ * qvl_rms_norm_i8: rows x hidden fp32 -> out (nullable) and/or its
+ * activation quantisation q/q_scales (nullable) for the next linear.
+ * Weight: INT8 [hidden] with fp32 scales [hidden / norm_group] (norm weights
+ * are always group-quantised by the exporter).  inplace_form selects the
+ * rms_norm_inplace rounding (1.0f/sqrtf) instead of rms_norm's
+ * (float)(1.0/sqrtf); the result is written to `out` either way.
+ * hidden <= 16384, hidden / quant_group <= 64. */
+int qvl_rms_norm_i8(const float *x, const int8_t *w, const float *w_scales, float *out,
+                    int16_t *q, float *q_scales, size_t rows, size_t hidden, size_t norm_group,
+                    float eps, int inplace_form, size_t quant_group, void *stream);
+/* embedding_lookup for an INT8 table with per-row scales (the tied
+ * embedding / LM-head matrix): out[t] = table[ids[t]] * row_scales[ids[t]]. */
+int qvl_embedding_lookup_i8(const int8_t *table, const float *row_scales, const int32_t *token_ids,
+                            float *out, size_t n_tokens, size_t vocab, size_t hidden, void *stream);
 
 /* ---- attention without a caller workspace -----------------------------
  * No counterpart in the reference.  Same inputs, outputs and result as

@@ -63,6 +63,8 @@ def lib():
         L.orc_argmax.argtypes = [_P, _Z]
         L.orc_argmax.restype = _I
         L.orc_rope_table.argtypes = [_P, _P, _Z, _I, ctypes.c_float]
+        L.orc_rms_norm_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, ctypes.c_float, _Z, _I]
+        L.orc_embedding_i8.argtypes = [_P, _P, _P, _Z, _Z]
         _orc = L
     return _orc
 
@@ -82,6 +84,9 @@ def ref_lib():
         L.ref_apply_rotary.argtypes = [_P, _P, _P, _Z, _I, _I, _I]
         L.ref_apply_rotary_cache.argtypes = [_P, _P, _P, _P, _Z, _I, _I, _I, _Z]
         L.ref_attention.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _Z, _I]
+        L.ref_rms_norm_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, ctypes.c_float, _Z]
+        L.ref_rms_norm_inplace_i8.argtypes = [_P, _P, _P, _Z, _Z, ctypes.c_float, _Z]
+        L.ref_embedding_i8.argtypes = [_P, _P, _P, _Z, _Z, _Z]
         _ref = L
     return _ref
 
@@ -161,7 +166,41 @@ def rope_table(S: int, D: int = 128, theta: float = 5e6):
     return c, s
 
 
+def rms_norm_i8(x, wq, ws, group_size, eps, inplace=False):
+    """x fp32 [batches, hidden] -> normalised copy (reference rms_norm /
+    rms_norm_inplace arithmetic)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    B, H = x.shape
+    out = np.empty_like(x)
+    lib().orc_rms_norm_i8(_ptr(x), _ptr(wq), _ptr(ws), _ptr(out), H, group_size, eps, B, int(inplace))
+    return out
+
+
+def embedding_i8(table, scales, token):
+    H = table.shape[1]
+    out = np.empty(H, np.float32)
+    lib().orc_embedding_i8(_ptr(table), _ptr(scales), _ptr(out), H, int(token))
+    return out
+
+
 # -------------------------------------------------------- compiled reference
+def ref_rms_norm_i8(x, wq, ws, group_size, eps, inplace=False):
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    B, H = x.shape
+    if inplace:
+        ref_lib().ref_rms_norm_inplace_i8(_ptr(x), _ptr(wq), _ptr(ws), H, group_size, eps, B)
+        return x
+    out = np.zeros_like(x)
+    ref_lib().ref_rms_norm_i8(_ptr(x), _ptr(wq), _ptr(ws), _ptr(out), H, group_size, eps, B)
+    return out
+
+
+def ref_embedding_i8(table, scales, token):
+    V, H = table.shape
+    out = np.zeros(H, np.float32)
+    ref_lib().ref_embedding_i8(_ptr(table), _ptr(scales), _ptr(out), V, H, int(token))
+    return out
+
 def ref_i8_kernel(x, w, ws, g):
     x = np.ascontiguousarray(x, dtype=np.float32)
     M, K = x.shape

@@ -259,3 +259,42 @@ void orc_rope_table(float *cos_tab, float *sin_tab, size_t S, int D, float theta
         }
     }
 }
+
+/* rms_norm / rms_norm_inplace with an INT8 group-quantised weight,
+ * layers/src/text_layer.cpp:111-147 and :234-272.  The reference's
+ * `#pragma omp simd reduction(+:ss)` compiles (g++ 13, AVX2) to 8 float lanes
+ * (lane l: x[8i+l]^2 added in i order, multiply and add rounded separately)
+ * whose lanes are then added in lane order; this was pinned against the
+ * compiled reference.  inv_rms: out-of-place (float)(1.0 / (double)sqrtf(a)),
+ * in place 1.0f / sqrtf(a), a = ss * (1/hidden) + eps (fused).
+ * out[j] = (float)wq[j] * ((ws[j/gs] * inv_rms) * x[j]). */
+void orc_rms_norm_i8(const float *x, const int8_t *wq, const float *ws, float *out,
+                     size_t hidden, size_t gs, float eps, size_t batches, int inplace) {
+    const float inv_hs = 1.0f / (float)hidden;
+    for (size_t b = 0; b < batches; ++b) {
+        const float *xr = x + b * hidden;
+        float *o = out + b * hidden;
+        float lane[8] = {0};
+        for (size_t i = 0; i < hidden; i += 8)
+            for (int l = 0; l < 8; ++l) {
+                float p = xr[i + l] * xr[i + l];
+                lane[l] = lane[l] + p;
+            }
+        float ss = 0.0f;
+        for (int l = 0; l < 8; ++l) ss = ss + lane[l];
+        float a = fmaf(ss, inv_hs, eps);
+        float inv = inplace ? 1.0f / sqrtf(a) : (float)(1.0 / (double)sqrtf(a));
+        for (size_t j = 0; j < hidden; ++j) {
+            float comb = ws[j / gs] * inv;
+            o[j] = (float)wq[j] * (comb * xr[j]);
+        }
+    }
+}
+
+/* embedding_lookup, layers/src/text_layer.cpp:41-48 (per-row scale). */
+void orc_embedding_i8(const int8_t *table, const float *scales, float *out, size_t hidden,
+                      size_t token) {
+    const int8_t *r = table + token * hidden;
+    const float s = scales[token];
+    for (size_t i = 0; i < hidden; ++i) out[i] = (float)r[i] * s;
+}

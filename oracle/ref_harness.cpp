@@ -103,3 +103,46 @@ void ref_attention(const float *key_cache, const float *value_cache, const float
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// layers/src/text_layer.cpp:52 `rms_norm`, INT8 group-quantised norm weight
+// (the exporter always group-quantises norms, export_qwen_bin.py:325).
+void ref_rms_norm_i8(const float *x, const int8_t *wq, const float *ws, float *out,
+                     size_t hidden, size_t group_size, float eps, size_t batches) {
+    QuietStdout qs;
+    Wrap xt({batches, hidden}, const_cast<float *>(x));
+    Wrap ot({batches, hidden}, out);
+    Tensor w({hidden}, const_cast<int8_t *>(wq), const_cast<float *>(ws), group_size, true,
+             DType::INT8, DType::FP32);
+    rms_norm(&xt.t, &w, &ot.t, eps, batches, 0);
+    w.buf = nullptr;
+    w.scale_buf = nullptr;
+}
+
+// layers/src/text_layer.cpp:177 `rms_norm_inplace`, INT8 group-quantised weight.
+void ref_rms_norm_inplace_i8(float *x, const int8_t *wq, const float *ws, size_t hidden,
+                             size_t group_size, float eps, size_t batches) {
+    QuietStdout qs;
+    Wrap xt({batches, hidden}, x);
+    Tensor w({hidden}, const_cast<int8_t *>(wq), const_cast<float *>(ws), group_size, true,
+             DType::INT8, DType::FP32);
+    rms_norm_inplace(&xt.t, &w, eps, batches, 0);
+    w.buf = nullptr;
+    w.scale_buf = nullptr;
+}
+
+// layers/src/text_layer.cpp:3 `embedding_lookup` for an INT8 table with
+// per-row scales (group_quantized = false).
+void ref_embedding_i8(const int8_t *table, const float *scales, float *out, size_t vocab,
+                      size_t hidden, size_t token) {
+    QuietStdout qs;
+    Wrap ot({hidden}, out);
+    Tensor e({vocab, hidden}, const_cast<int8_t *>(table), const_cast<float *>(scales), hidden, false,
+             DType::INT8, DType::FP32);
+    embedding_lookup(&e, &ot.t, token, hidden);
+    e.buf = nullptr;
+    e.scale_buf = nullptr;
+}
+
+}  // extern "C"

@@ -42,7 +42,10 @@ EXPORTED = (
     "qvl_linear_i8_workspace_bytes", "qvl_linear_i8", "qvl_linear_q16_i8", "qvl_swiglu",
     "qvl_swiglu_mlp_workspace_bytes", "qvl_swiglu_mlp_i8", "qvl_rope_kv_append",
     "qvl_attention_workspace_bytes", "qvl_attention_decode", "qvl_argmax_rows",
+    "qvl_qknorm_rope_kv_append", "qvl_rms_norm_i8", "qvl_embedding_lookup_i8",
+    "qvl_swiglu_quantize_rows",
 )
+SEM_ACCUMULATE = 0x100
 
 
 class QvlError(RuntimeError):
@@ -84,6 +87,11 @@ def load_library(path: str = LIB_PATH):
     L.qvl_attention_workspace_bytes.argtypes = [_Z, _I, ctypes.POINTER(AttnDims)]
     L.qvl_attention_decode.argtypes = [_P] * 6 + [_Z, _I, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
     L.qvl_argmax_rows.argtypes = [_P, _P, _Z, _Z, _P]
+    L.qvl_qknorm_rope_kv_append.argtypes = [_P] * 8 + [_Z, _P, _P, _P, _P, _P, _P, _Z, ctypes.c_float,
+                                                       ctypes.POINTER(AttnDims), _P]
+    L.qvl_rms_norm_i8.argtypes = [_P] * 6 + [_Z, _Z, _Z, ctypes.c_float, _I, _Z, _P]
+    L.qvl_embedding_lookup_i8.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
+    L.qvl_swiglu_quantize_rows.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
     _lib = L
     return L
 
@@ -251,3 +259,41 @@ def greedy_decode(logits: torch.Tensor, out=None, stream=None) -> torch.Tensor:
     _check(load_library().qvl_argmax_rows(_ptr(logits), _ptr(out), rows, n, _stream(stream)),
            "greedy_decode")
     return out
+
+
+def rms_norm_i8(x, w, w_scales, norm_group, eps, out=None, q=None, q_scales=None, quant_group=0,
+                inplace_form=False, stream=None):
+    """rms_norm (inplace_form=False) / rms_norm_inplace rounding with an INT8
+    group-quantised weight; writes `out` and/or the next linear's int16
+    activations q, q_scales (group quant_group)."""
+    rows, H = x.shape
+    _check(load_library().qvl_rms_norm_i8(_ptr(x), _ptr(w), _ptr(w_scales), _ptr(out), _ptr(q),
+                                          _ptr(q_scales), rows, H, norm_group, eps, int(inplace_form),
+                                          quant_group, _stream(stream)), "rms_norm_i8")
+    return out
+
+
+def qknorm_rope_kv_append(q, k_new, v_new, kv: PagedKV, seq_ids, positions, rope_cos, rope_sin,
+                          q_norm_w, q_norm_s, k_norm_w, k_norm_s, norm_group, eps, stream=None):
+    nq = q.shape[0]
+    _check(load_library().qvl_qknorm_rope_kv_append(
+        _ptr(q), _ptr(k_new), _ptr(v_new), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table),
+        _ptr(seq_ids), _ptr(positions), nq, _ptr(rope_cos), _ptr(rope_sin), _ptr(q_norm_w),
+        _ptr(q_norm_s), _ptr(k_norm_w), _ptr(k_norm_s), norm_group, eps, ctypes.byref(kv.dims),
+        _stream(stream)), "qknorm_rope_kv_append")
+    return q
+
+
+def embedding_lookup_i8(table, row_scales, token_ids, out, stream=None):
+    V, H = table.shape
+    _check(load_library().qvl_embedding_lookup_i8(_ptr(table), _ptr(row_scales), _ptr(token_ids), _ptr(out),
+                                                  token_ids.numel(), V, H, _stream(stream)),
+           "embedding_lookup_i8")
+    return out
+
+
+def swiglu_quantize_rows(gate, up, q, q_scales, group_size, stream=None):
+    M, I = gate.shape
+    _check(load_library().qvl_swiglu_quantize_rows(_ptr(gate), _ptr(up), _ptr(q), _ptr(q_scales), M, I,
+                                                   group_size, _stream(stream)), "swiglu_quantize_rows")
+    return q

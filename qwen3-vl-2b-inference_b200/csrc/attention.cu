@@ -54,43 +54,82 @@ __device__ __forceinline__ void h8_to_f8(const uint4 &v, float f[8]) {
 }  // namespace
 
 // ---------------------------------------------------------------- RoPE + append
-// grid: nq; block 256.  Pairs (i, i + D/2): y1 = x1*c - (x2*s) fused,
-// y2 = x1*s + (x2*c) fused, exactly as apply_rotary's fmsub/fmadd.
+// grid: nq; block 256; dynamic smem (NH + NKV) * D floats.
+// Optional QK-norm first (rms_norm_inplace with the per-layer INT8 q_norm /
+// k_norm weights, model/src/forward.cpp:531-538, arithmetic of
+// layers/src/text_layer.cpp:234-272), then RoPE on pairs (i, i + D/2):
+// y1 = x1*c - (x2*s) fused, y2 = x1*s + (x2*c) fused, exactly as
+// apply_rotary's fmsub/fmadd.  q is rotated in place; k (rotated) and v are
+// rounded to fp16 and written at the query's position.
 __global__ void rope_append_kernel(float *__restrict q, const float *__restrict k_new,
                                    const float *__restrict v_new, uint16_t *__restrict k_pages,
                                    uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
                                    const int32_t *__restrict seq_ids, const int32_t *__restrict positions,
                                    const float *__restrict rope_cos, const float *__restrict rope_sin,
-                                   Dims d) {
+                                   QkNorm nrm, Dims d) {
+    extern __shared__ __align__(16) float hs[];
+    __shared__ float red[64 * 8];
+    __shared__ float invh[64];
     pdl_launch_dependents();
     pdl_wait();
     const int i = blockIdx.x;
     const int pos = positions[i];
     if (pos < 0 || pos >= d.max_pos) return;
     constexpr int half = kD / 2;
+    const bool has_k = k_new != nullptr;
+    const int nh = d.NH + (has_k ? d.NKV : 0);
+    float *qi = q + (size_t)i * d.NH * kD;
+    const float *ki = has_k ? k_new + (size_t)i * d.NKV * kD : nullptr;
+    for (int e = threadIdx.x; e < nh * kD; e += blockDim.x)
+        hs[e] = (e < d.NH * kD) ? qi[e] : ki[e - d.NH * kD];
+    __syncthreads();
+    if (nrm.q_w) {
+        for (int t = threadIdx.x; t < nh * 8; t += blockDim.x) {
+            const int h = t >> 3, l = t & 7;
+            const float *xh = hs + h * kD;
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kD; j += 8) acc = add_rn(acc, mul_rn(xh[j + l], xh[j + l]));
+            red[t] = acc;
+        }
+        __syncthreads();
+        for (int h = threadIdx.x; h < nh; h += blockDim.x) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int l = 0; l < 8; ++l) ss = add_rn(ss, red[h * 8 + l]);
+            const float a = fma_rn(ss, __fdiv_rn(1.0f, (float)kD), nrm.eps);
+            invh[h] = __fdiv_rn(1.0f, __fsqrt_rn(a));
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nh * kD; e += blockDim.x) {
+            const int h = e / kD, j = e - h * kD;
+            const bool isq = h < d.NH;
+            const int8_t *w = isq ? nrm.q_w : nrm.k_w;
+            const float *ws = isq ? nrm.q_s : nrm.k_s;
+            hs[e] = mul_rn((float)w[j], mul_rn(mul_rn(ws[j / nrm.gs], invh[h]), hs[e]));
+        }
+        __syncthreads();
+    }
     const float *c = rope_cos + (size_t)pos * half;
     const float *s = rope_sin + (size_t)pos * half;
-    // q heads, in place
-    float *qi = q + (size_t)i * d.NH * kD;
     for (int e = threadIdx.x; e < d.NH * half; e += blockDim.x) {
         const int h = e / half, j = e - h * half;
-        float *x = qi + h * kD;
-        float x1 = x[j], x2 = x[j + half];
-        x[j] = fma_rn(x1, c[j], -mul_rn(x2, s[j]));
-        x[j + half] = fma_rn(x1, s[j], mul_rn(x2, c[j]));
+        const float *x = hs + h * kD;
+        const float x1 = x[j], x2 = x[j + half];
+        qi[h * kD + j] = fma_rn(x1, c[j], -mul_rn(x2, s[j]));
+        qi[h * kD + j + half] = fma_rn(x1, s[j], mul_rn(x2, c[j]));
     }
-    if (k_new == nullptr) return;
+    if (!has_k) return;
     const int32_t *pt_row = page_table + (size_t)seq_ids[i] * d.maxp;
     const int page = pt_row[pos / d.P];
     const int slot = pos % d.P;
-    const float *ki = k_new + (size_t)i * d.NKV * kD;
     const float *vi = v_new + (size_t)i * d.NKV * kD;
     for (int e = threadIdx.x; e < d.NKV * half; e += blockDim.x) {
         const int h = e / half, j = e - h * half;
-        const float *x = ki + h * kD;
-        float x1 = x[j], x2 = x[j + half];
-        float y1 = fma_rn(x1, c[j], -mul_rn(x2, s[j]));
-        float y2 = fma_rn(x1, s[j], mul_rn(x2, c[j]));
+        const float *x = hs + (d.NH + h) * kD;
+        const float x1 = x[j], x2 = x[j + half];
+        const float y1 = fma_rn(x1, c[j], -mul_rn(x2, s[j]));
+        const float y2 = fma_rn(x1, s[j], mul_rn(x2, c[j]));
         const size_t off = (((size_t)page * d.NKV + h) * d.P + slot) * kD;
         k_pages[off + j] = __half_as_ushort(__float2half_rn(y1));
         k_pages[off + j + half] = __half_as_ushort(__float2half_rn(y2));
@@ -398,9 +437,18 @@ cudaError_t launch_attention(const AttnArgs &a, void *workspace, cudaStream_t st
 
 cudaError_t launch_rope_append(const RopeArgs &a, cudaStream_t stream) {
     Dims d{a.NH, a.NKV, a.P, a.maxp, a.max_pos};
-    return launch_pdl(rope_append_kernel, dim3((unsigned)a.nq), dim3(256), stream, a.q, a.k_new,
-                      a.v_new, a.k_pages, a.v_pages, a.page_table, a.seq_ids, a.positions,
-                      a.rope_cos, a.rope_sin, d);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.nq);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)(a.NH + a.NKV) * kD * sizeof(float);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rope_append_kernel, a.q, a.k_new, a.v_new, a.k_pages, a.v_pages,
+                              a.page_table, a.seq_ids, a.positions, a.rope_cos, a.rope_sin, a.norm, d);
 }
 
 }  // namespace qvl

@@ -15,6 +15,16 @@ struct AttnArgs {
     int NH, NKV, P, maxp, max_pos;
 };
 
+// Optional per-layer QK-norm: INT8 weights [D] with fp32 group scales.
+struct QkNorm {
+    const int8_t *q_w;   // nullptr: no QK-norm
+    const float *q_s;
+    const int8_t *k_w;
+    const float *k_s;
+    int gs;
+    float eps;
+};
+
 struct RopeArgs {
     float *q;
     const float *k_new, *v_new;
@@ -23,6 +33,7 @@ struct RopeArgs {
     size_t nq;
     const float *rope_cos, *rope_sin;
     int NH, NKV, P, maxp, max_pos;
+    QkNorm norm;
 };
 
 // Split-K scratch: raw scores, chunk maxima, chunk sums, chunk partial outputs.

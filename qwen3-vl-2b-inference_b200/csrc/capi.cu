@@ -10,6 +10,7 @@
 #include "swiglu.cuh"
 #include "attention.cuh"
 #include "argmax.cuh"
+#include "norm.cuh"
 
 namespace {
 int g_last_cuda_error = 0;
@@ -38,8 +39,8 @@ bool lane8_for(int semantics, size_t M, size_t N, size_t K) {
 // y[M,N] from pre-quantised activations: CUDA-core GEMV for small M (and for
 // the LANE8 summation order at any M), tensor cores for TILED at M >= 16.
 int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const float *Bs, float *C,
-                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st) {
-    if (!lane8 && qvl::gemm_tc_supported(M, N, K, g)) {
+                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st, int acc = 0) {
+    if (!lane8 && !acc && qvl::gemm_tc_supported(M, N, K, g)) {
         QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, B, Bs, C, (int)M, (int)N, (int)K, (int)g, st));
         return QVL_OK;
     }
@@ -58,6 +59,7 @@ int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const flo
         a.K = (int)K;
         a.g = (int)g;
         a.ldy = (long)N;
+        a.acc = acc;
         QVL_CUDA_TRY(qvl::launch_gemv_i8(a, lane8, st));
     }
     return QVL_OK;
@@ -112,9 +114,11 @@ int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
     int rc = check_linear_shape(M, N, K, group_size);
     if (rc) return rc;
     if (!aligned(q, 16) || !aligned(B, 16) || (K * sizeof(int8_t)) % 16) return QVL_ERR_INVALID;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    semantics &= ~QVL_SEM_ACCUMULATE;
     if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
     return run_q16_linear(q, q_scales, B, B_scales, C, M, N, K, group_size,
-                          lane8_for(semantics, M, N, K), (cudaStream_t)stream);
+                          lane8_for(semantics, M, N, K), (cudaStream_t)stream, acc);
 }
 
 int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float *C, size_t M,
@@ -124,6 +128,8 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     const size_t g = group_quantized ? group_size : K;
     int rc = check_linear_shape(M, N, K, g);
     if (rc) return rc;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    semantics &= ~QVL_SEM_ACCUMULATE;
     if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
     const size_t need = qbuf_bytes(M, K, g);
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
@@ -132,7 +138,7 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     float *qs = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * K * 2));
     cudaStream_t st = (cudaStream_t)stream;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
-    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st);
+    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st, acc);
 }
 
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
@@ -205,7 +211,67 @@ int qvl_rope_kv_append(float *q, const float *k_new, const float *v_new, uint16_
     a.rope_cos = rope_cos; a.rope_sin = rope_sin;
     a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
     a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    a.norm = qvl::QkNorm{nullptr, nullptr, nullptr, nullptr, 1, 0.0f};
     QVL_CUDA_TRY(qvl::launch_rope_append(a, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_qknorm_rope_kv_append(float *q, const float *k_new, const float *v_new, uint16_t *k_pages,
+                              uint16_t *v_pages, const int32_t *page_table, const int32_t *seq_ids,
+                              const int32_t *positions, size_t nq, const float *rope_cos,
+                              const float *rope_sin, const int8_t *q_norm_w, const float *q_norm_s,
+                              const int8_t *k_norm_w, const float *k_norm_s, size_t norm_group,
+                              float eps, const qvl_attn_dims *dims, void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !k_new || !v_new || !k_pages || !v_pages || !page_table || !seq_ids || !positions ||
+        !rope_cos || !rope_sin || !q_norm_w || !q_norm_s || !k_norm_w || !k_norm_s)
+        return QVL_ERR_INVALID;
+    if (norm_group == 0 || 128 % norm_group || dims->num_heads + dims->num_kv_heads > 64) return QVL_ERR_UNSUPPORTED;
+    if (nq == 0) return QVL_OK;
+    qvl::RopeArgs a;
+    a.q = q; a.k_new = k_new; a.v_new = v_new; a.k_pages = k_pages; a.v_pages = v_pages;
+    a.page_table = page_table; a.seq_ids = seq_ids; a.positions = positions; a.nq = nq;
+    a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    a.norm = qvl::QkNorm{q_norm_w, q_norm_s, k_norm_w, k_norm_s, (int)norm_group, eps};
+    QVL_CUDA_TRY(qvl::launch_rope_append(a, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_rms_norm_i8(const float *x, const int8_t *w, const float *w_scales, float *out,
+                    int16_t *q, float *q_scales, size_t rows, size_t hidden, size_t norm_group,
+                    float eps, int inplace_form, size_t quant_group, void *stream) {
+    if (!x || !w || !w_scales || (!out && !q) || (q && !q_scales)) return QVL_ERR_INVALID;
+    if (rows == 0) return QVL_OK;
+    if (hidden == 0 || hidden % 16 || hidden > 16384 || norm_group == 0 || hidden % norm_group)
+        return QVL_ERR_INVALID;
+    if (!aligned(x, 16)) return QVL_ERR_INVALID;
+    if (q && (quant_group == 0 || quant_group % 16 || hidden % quant_group || hidden / quant_group > 64))
+        return QVL_ERR_UNSUPPORTED;
+    QVL_CUDA_TRY(qvl::launch_rmsnorm_quant(x, w, w_scales, out, q, q_scales, (int)rows, (int)hidden,
+                                           (int)norm_group, eps, inplace_form != 0,
+                                           q ? (int)quant_group : 16, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, float *q_scales,
+                             size_t M, size_t I, size_t group_size, void *stream) {
+    if (!gate || !up || !q || !q_scales) return QVL_ERR_INVALID;
+    if (M == 0) return QVL_OK;
+    if (group_size == 0 || group_size % 16 || I % group_size) return QVL_ERR_INVALID;
+    QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, q, q_scales, (int)M, (int)I, (int)group_size,
+                                          (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_embedding_lookup_i8(const int8_t *table, const float *row_scales, const int32_t *token_ids,
+                            float *out, size_t n_tokens, size_t vocab, size_t hidden, void *stream) {
+    if (!table || !row_scales || !token_ids || !out || vocab == 0 || hidden == 0) return QVL_ERR_INVALID;
+    if (n_tokens == 0) return QVL_OK;
+    QVL_CUDA_TRY(qvl::launch_embedding_i8(table, row_scales, token_ids, out, (int)n_tokens, (int)hidden,
+                                          (int)vocab, (cudaStream_t)stream));
     return QVL_OK;
 }
 

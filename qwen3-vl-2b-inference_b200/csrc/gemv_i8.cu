@@ -40,7 +40,7 @@ template <int MR, bool LANE, int IT>
 __global__ void __launch_bounds__(kThreads, fast_min_blocks<MR, IT>())
 gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
                     const int8_t *__restrict W, const float *__restrict ws, float *__restrict y,
-                    int M, int N, int K, int g, long ldy, int seglog) {
+                    int M, int N, int K, int g, long ldy, int acc, int seglog) {
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *q_s = reinterpret_cast<int16_t *>(smem);
     const int G = K / g;
@@ -185,7 +185,10 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
                 float p = add_rn(u, __shfl_xor_sync(full, u, d3));
                 out = add_rn(p, __shfl_xor_sync(full, p, d2));
             }
-            if (lane == 0) y[(long)m * ldy + n] = out;
+            if (lane == 0) {
+                float *yp = y + (long)m * ldy + n;
+                *yp = acc ? add_rn(*yp, out) : out;   // residual add: add_vector order
+            }
         }
         if constexpr (kDouble) {
 #pragma unroll
@@ -229,7 +232,7 @@ cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy,
+    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy, a.acc,
                               seglog);
 }
 

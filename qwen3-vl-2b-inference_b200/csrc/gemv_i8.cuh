@@ -13,6 +13,7 @@ struct GemvArgs {
     float *y;           // [M, ldy]
     int M, N, K, g;
     long ldy;
+    int acc;            // 1: y += result (fused residual add), 0: y = result
 };
 
 bool gemv_shape_supported(int K, int g);

@@ -32,7 +32,7 @@ template <int MR, bool LANE, int SEGLOG>
 __global__ void __launch_bounds__(kThreads)
 gemv_i8_kernel(const int16_t *__restrict q, const float *__restrict qs,
                const int8_t *__restrict W, const float *__restrict ws, float *__restrict y,
-               int M, int N, int K, int g, long ldy) {
+               int M, int N, int K, int g, long ldy, int acc) {
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *q_s = reinterpret_cast<int16_t *>(smem);
     const int G = K / g;
@@ -204,7 +204,10 @@ gemv_i8_kernel(const int16_t *__restrict q, const float *__restrict qs,
                     } else {
                         out = st.cf[m];
                     }
-                    if (lane == 0) y[(long)m * ldy + n] = out;
+                    if (lane == 0) {
+                float *yp = y + (long)m * ldy + n;
+                *yp = acc ? add_rn(*yp, out) : out;   // residual add: add_vector order
+            }
                 }
                 reset_row();
             }
@@ -243,7 +246,7 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy);
+    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy, a.acc);
 }
 
 template <int MR, bool LANE>

@@ -1,0 +1,143 @@
+// RMSNorm with an INT8 group-quantised weight (the exporter always
+// group-quantises norm weights, export_bin/export_qwen_bin.py:325), fused with
+// the activation quantisation of the linear that consumes its output, and the
+// INT8 embedding lookup.
+//
+// Reference arithmetic (layers/src/text_layer.cpp:111-147 rms_norm,
+// :234-272 rms_norm_inplace), pinned against the compiled reference: the sum
+// of squares is 8 float lanes (lane l accumulates x[8i+l]^2, multiply and add
+// rounded separately) added in lane order; a = ss * (1/H) + eps (fused);
+// inv_rms = (float)(1.0 / (double)sqrtf(a)) for rms_norm and 1.0f / sqrtf(a)
+// for rms_norm_inplace; out[j] = (float)wq[j] * ((ws[j/gs] * inv_rms) * x[j]).
+#include "common.cuh"
+#include "qact.cuh"
+#include "norm.cuh"
+
+namespace qvl {
+
+// Sum of squares in the reference's lane order, by warp 0 of the CTA; the
+// result is valid in every lane of warp 0.
+__device__ __forceinline__ float rms_sumsq_ref(const float *xs, int H) {
+    const int lane = threadIdx.x & 31;
+    const int l = lane & 7;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < H; i += 8) {
+        const float v = xs[i + l];
+        acc = add_rn(acc, mul_rn(v, v));
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss = add_rn(ss, __shfl_sync(0xffffffffu, acc, k));
+    return ss;
+}
+
+__device__ __forceinline__ float rms_inv(float ss, int H, float eps, bool inplace_form) {
+    const float inv_hs = __fdiv_rn(1.0f, (float)H);
+    const float a = fma_rn(ss, inv_hs, eps);
+    const float r = __fsqrt_rn(a);
+    return inplace_form ? __fdiv_rn(1.0f, r) : __double2float_rn(1.0 / (double)r);
+}
+
+// grid: rows; block 256; dynamic smem 2*H floats.
+// out (nullable) receives the normalised row; q/qs (nullable) its
+// quantisation with group qg (bit-exact with quantize_rows on `out`).
+__global__ void __launch_bounds__(256)
+rmsnorm_quant_kernel(const float *__restrict x, const int8_t *__restrict wq,
+                     const float *__restrict ws, float *__restrict out, int16_t *__restrict q,
+                     float *__restrict qs, int H, int ngs, float eps, int inplace_form, int qg) {
+    extern __shared__ __align__(16) float sm[];
+    float *xs = sm;
+    float *ts = sm + H;
+    __shared__ float inv_sh;
+    __shared__ float qinv[64];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int row = blockIdx.x;
+    const float *xr = x + (size_t)row * H;
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(xr)[i];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float ss = rms_sumsq_ref(xs, H);
+        if (threadIdx.x == 0) inv_sh = rms_inv(ss, H, eps, inplace_form != 0);
+    }
+    __syncthreads();
+    const float inv = inv_sh;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+        const float t = mul_rn((float)wq[j], mul_rn(mul_rn(ws[j / ngs], inv), xs[j]));
+        ts[j] = t;
+        if (out) out[(size_t)row * H + j] = t;
+    }
+    if (!q) return;
+    __syncthreads();
+    const int G = H / qg;
+    const int hw = threadIdx.x >> 4, nhw = blockDim.x >> 4, t16 = threadIdx.x & 15;
+    // both half-warps of a warp take the same trip count (full-mask shuffles)
+    for (int e0 = hw & ~1; e0 < G; e0 += nhw) {
+        const int e_raw = e0 + (hw & 1);
+        const bool active = e_raw < G;
+        const int e = active ? e_raw : e0;
+        const float s = group_scale_ref(ts + (size_t)e * qg, qg, t16);
+        if (active && t16 == 0) {
+            qs[(size_t)row * G + e] = s;
+            qinv[e] = __fdiv_rn(1.0f, s);
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < H; j += blockDim.x)
+        q[(size_t)row * H + j] = quant_one(ts[j], qinv[j / qg]);
+}
+
+// grid: n_tokens; block 256.  out[t] = (float)table[id] * scale[id]
+// (embedding_lookup, per-row scales, layers/src/text_layer.cpp:41-48).
+__global__ void embedding_i8_kernel(const int8_t *__restrict table, const float *__restrict scales,
+                                    const int32_t *__restrict ids, float *__restrict out, int H,
+                                    int vocab) {
+    pdl_launch_dependents();
+    pdl_wait();
+    int id = ids[blockIdx.x];
+    if (id < 0 || id >= vocab) id = 0;
+    const int8_t *r = table + (size_t)id * H;
+    const float s = scales[id];
+    for (int j = threadIdx.x; j < H; j += blockDim.x)
+        out[(size_t)blockIdx.x * H + j] = mul_rn((float)r[j], s);
+}
+
+static void pdl_attr(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStream_t st) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.stream = st;
+}
+
+cudaError_t launch_rmsnorm_quant(const float *x, const int8_t *wq, const float *ws, float *out,
+                                 int16_t *q, float *qs, int rows, int H, int ngs, float eps,
+                                 bool inplace_form, int qg, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    pdl_attr(cfg, attr, st);
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)2 * H * sizeof(float);
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)cfg.dynamicSmemBytes);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, wq, ws, out, q, qs, H, ngs, eps,
+                              inplace_form ? 1 : 0, qg);
+}
+
+cudaError_t launch_embedding_i8(const int8_t *table, const float *scales, const int32_t *ids, float *out,
+                                int n, int H, int vocab, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    pdl_attr(cfg, attr, st);
+    cfg.gridDim = dim3(n);
+    cfg.blockDim = dim3(256);
+    return cudaLaunchKernelEx(&cfg, embedding_i8_kernel, table, scales, ids, out, H, vocab);
+}
+
+}  // namespace qvl

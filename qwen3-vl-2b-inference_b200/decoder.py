@@ -1,0 +1,208 @@
+"""Qwen3-VL-2B text decoder step on the sm_100a kernels.
+
+Host orchestration of one decode token for B independent requests, in the
+order of the reference's ``forward_text`` (model/src/forward.cpp:458-720):
+
+    embedding_lookup -> 28 x [rms_norm -> q/k/v linear -> QK rms_norm_inplace
+    -> RoPE + KV append -> attention -> o linear + residual -> rms_norm ->
+    gate/up linear -> swiglu -> down linear + residual] -> rms_norm_inplace ->
+    tied LM head -> greedy_decode
+
+Every product runs through the C ABI (libqvl_b200.so).  Row i of every linear
+is computed in the reference's M=1 summation order (QVL_SEM_LANE8), so each
+request matches the reference run on that request alone.  Differences from
+the reference, by design: the KV cache is FP16 and paged (the reference keeps
+an FP32 contiguous cache, load_model.cpp:348-349) and attention is split-K
+over the context (same exp polynomial and zeroing rules).
+
+Weights use the reference layout (export_bin/export_qwen_bin.py): int8
+[out, in] per matrix with per-output-row fp32 scales (per-row export), norm
+weights int8 with fp32 group scales (group ``norm_group``).  ``random()``
+draws them synthetically (no checkpoint is available): int8 ~U[-127,127],
+scales ~U(0.001, 0.02).
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+import torch
+
+from . import (SEM_ACCUMULATE, SEM_LANE8, PagedKV, Workspace, attention, embedding_lookup_i8,
+               greedy_decode, linear_q16, qknorm_rope_kv_append, rms_norm_i8, swiglu_quantize_rows)
+from . import load_library
+
+
+@dataclasses.dataclass
+class TextConfig:
+    hidden: int = 2048
+    intermediate: int = 6144
+    layers: int = 28
+    heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 128
+    vocab: int = 151936
+    eps: float = 1e-6
+    rope_theta: float = 5e6
+    norm_group: int = 128
+
+
+def rope_table(max_pos: int, head_dim: int = 128, theta: float = 5e6):
+    """Text section of qwen_rope_precompute (model/src/load_model.cpp:428-472):
+    cos/sin of pos * 1/theta^(2i/D), computed on the host in float32."""
+    i = np.arange(head_dim // 2, dtype=np.float32)
+    inv_freq = (np.float32(1.0) / np.power(np.float32(theta), (np.float32(2.0) * i) / np.float32(head_dim),
+                                           dtype=np.float32)).astype(np.float32)
+    pos = np.arange(max_pos, dtype=np.float32)[:, None]
+    f = (pos * inv_freq[None, :]).astype(np.float32)
+    return np.cos(f).astype(np.float32), np.sin(f).astype(np.float32)
+
+
+_MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
+
+
+class TextWeights:
+    """Device copies of the text-decoder weights in the reference layout."""
+
+    def __init__(self, cfg: TextConfig, tensors: dict):
+        self.cfg = cfg
+        self.t = tensors
+
+    @staticmethod
+    def shapes(cfg: TextConfig):
+        H, I, L, D = cfg.hidden, cfg.intermediate, cfg.layers, cfg.head_dim
+        return {"wq": (L, cfg.heads * D, H), "wk": (L, cfg.kv_heads * D, H), "wv": (L, cfg.kv_heads * D, H),
+                "wo": (L, H, cfg.heads * D), "wg": (L, I, H), "wu": (L, I, H), "wd": (L, H, I)}
+
+    @classmethod
+    def random(cls, cfg: TextConfig, seed: int = 0, device="cuda"):
+        g = torch.Generator(device=device).manual_seed(seed)
+        t = {}
+
+        def i8(shape):
+            return torch.randint(-127, 128, shape, dtype=torch.int8, device=device, generator=g)
+
+        def sc(shape):
+            return (torch.rand(shape, dtype=torch.float32, device=device, generator=g) * 0.019 + 0.001)
+
+        for name, shp in cls.shapes(cfg).items():
+            t[name] = i8(shp)
+            t[name + "_s"] = sc(shp[:2])                      # per-output-row scales
+        H, L, D, ng = cfg.hidden, cfg.layers, cfg.head_dim, cfg.norm_group
+        for name, n in (("in_norm", H), ("post_norm", H), ("q_norm", D), ("k_norm", D)):
+            t[name] = i8((L, n))
+            t[name + "_s"] = sc((L, n // ng))
+        t["final_norm"] = i8((H,))
+        t["final_norm_s"] = sc((H // ng,))
+        t["embed"] = i8((cfg.vocab, H))                       # tied with the LM head
+        t["embed_s"] = sc((cfg.vocab,))
+        return cls(cfg, t)
+
+    def numpy(self):
+        return {k: v.cpu().numpy() for k, v in self.t.items()}
+
+
+class TextDecoder:
+    """Batched decode over a paged FP16 KV cache (one sequence per request)."""
+
+    def __init__(self, weights: TextWeights, max_batch: int, max_ctx: int, page_size: int = 64,
+                 device="cuda"):
+        self.w = weights
+        cfg = self.cfg = weights.cfg
+        self.B = max_batch
+        self.max_ctx = max_ctx
+        dev = self.device = torch.device(device)
+        H, I, D = cfg.hidden, cfg.intermediate, cfg.head_dim
+        B = max_batch
+        f32, i16 = torch.float32, torch.int16
+        self.x = torch.zeros((B, H), dtype=f32, device=dev)
+        self.qx = torch.zeros((B, H), dtype=i16, device=dev)
+        self.qx_s = torch.zeros((B, 1), dtype=f32, device=dev)
+        self.q = torch.zeros((B, cfg.heads * D), dtype=f32, device=dev)
+        self.k = torch.zeros((B, cfg.kv_heads * D), dtype=f32, device=dev)
+        self.v = torch.zeros((B, cfg.kv_heads * D), dtype=f32, device=dev)
+        self.att = torch.zeros((B, cfg.heads * D), dtype=f32, device=dev)
+        self.qa = torch.zeros((B, cfg.heads * D), dtype=i16, device=dev)
+        self.qa_s = torch.zeros((B, 1), dtype=f32, device=dev)
+        self.gate = torch.zeros((B, I), dtype=f32, device=dev)
+        self.up = torch.zeros((B, I), dtype=f32, device=dev)
+        self.qh = torch.zeros((B, I), dtype=i16, device=dev)
+        self.qh_s = torch.zeros((B, 1), dtype=f32, device=dev)
+        self.logits = torch.zeros((B, cfg.vocab), dtype=f32, device=dev)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.seq_ids = torch.arange(B, dtype=torch.int32, device=dev)
+        self.kv = [PagedKV(B, max_ctx, cfg.heads, cfg.kv_heads, D, page_size, max_pos=max_ctx, device=dev)
+                   for _ in range(cfg.layers)]
+        cos, sin = rope_table(max_ctx, D, cfg.rope_theta)
+        self.set_rope_table(cos, sin)
+        self.ws = Workspace(dev)
+        self.ws.get(load_library().qvl_attention_workspace_bytes(B, max_ctx, self.kv[0].dims))
+
+    def set_rope_table(self, cos: np.ndarray, sin: np.ndarray):
+        self.rope_cos = torch.from_numpy(np.ascontiguousarray(cos)).to(self.device)
+        self.rope_sin = torch.from_numpy(np.ascontiguousarray(sin)).to(self.device)
+
+    def _lin(self, q, qs, name, l, out, acc=False):
+        t = self.w.t
+        W = t[name][l] if l is not None else t[name]
+        S = t[name + "_s"][l] if l is not None else t[name + "_s"]
+        return linear_q16(q, qs, W, S, q.shape[1], C=out, semantics=SEM_LANE8 | (SEM_ACCUMULATE if acc else 0))
+
+    def step(self, B=None):
+        """One decode token for requests 0..B-1: reads self.tokens and
+        self.positions, leaves the logits in self.logits and the greedy
+        tokens in self.tokens, and advances self.positions by one.  Only
+        device work is issued (graph-capturable)."""
+        B = B or self.B
+        cfg, t = self.cfg, self.w.t
+        H, ng, eps = cfg.hidden, cfg.norm_group, cfg.eps
+        x = self.x[:B]
+        qx, qx_s = self.qx[:B], self.qx_s[:B]
+        seq, pos = self.seq_ids[:B], self.positions[:B]
+        embedding_lookup_i8(t["embed"], t["embed_s"], self.tokens[:B], x)
+        for l in range(cfg.layers):
+            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+            self._lin(qx, qx_s, "wq", l, self.q[:B])
+            self._lin(qx, qx_s, "wk", l, self.k[:B])
+            self._lin(qx, qx_s, "wv", l, self.v[:B])
+            qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
+                                  self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
+                                  t["k_norm_s"][l], ng, eps)
+            attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+            _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
+            self._lin(self.qa[:B], self.qa_s[:B], "wo", l, x, acc=True)
+            rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+            self._lin(qx, qx_s, "wg", l, self.gate[:B])
+            self._lin(qx, qx_s, "wu", l, self.up[:B])
+            swiglu_quantize_rows(self.gate[:B], self.up[:B], self.qh[:B], self.qh_s[:B], cfg.intermediate)
+            self._lin(self.qh[:B], self.qh_s[:B], "wd", l, x, acc=True)
+        rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s, quant_group=H,
+                    inplace_form=True)
+        self._lin(qx, qx_s, "embed", None, self.logits[:B])
+        greedy_decode(self.logits[:B], out=self.tokens[:B])
+        pos.add_(1)
+
+    # launches of our kernels per step (attention = 3 kernels)
+    def kernels_per_step(self):
+        return 1 + self.cfg.layers * (1 + 3 + 1 + 3 + 1 + 1 + 1 + 2 + 1 + 1) + 1 + 1 + 1
+
+
+def _quantize_into(x, q, qs):
+    from . import _check, _ptr, _stream
+    M, K = x.shape
+    _check(load_library().qvl_quantize_rows(_ptr(x), _ptr(q), _ptr(qs), M, K, K, _stream(None)), "quantize_rows")
+
+
+def fill_kv_random(dec: TextDecoder, ctx: int, seed: int = 0):
+    """Synthetic prompt state: positions [0, ctx) of every request's cache
+    hold fp16 N(0,1) keys/values (stands in for a prefilled prompt)."""
+    g = torch.Generator(device=dec.device).manual_seed(seed)
+    P = dec.kv[0].page_size
+    npages = (ctx + P - 1) // P
+    for kv in dec.kv:
+        for b in range(dec.B):
+            pages = kv.page_table[b, :npages].long()
+            kv.k[pages] = torch.randn(kv.k[pages].shape, generator=g, device=dec.device).half()
+            kv.v[pages] = torch.randn(kv.v[pages].shape, generator=g, device=dec.device).half()
+    dec.positions.fill_(ctx)

@@ -117,3 +117,23 @@ def test_softmax_swiglu_vs_compiled_reference():
     g = rng.standard_normal(6144, dtype=np.float32) * 5
     u = rng.standard_normal(6144, dtype=np.float32)
     np.testing.assert_array_equal(oracle.swiglu(g, u), oracle.ref_swiglu(g, u))
+
+
+@ref
+@pytest.mark.parametrize("H,gs,B", [(2048, 128, 3), (128, 128, 24), (128, 64, 16), (6144, 128, 1)])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_rms_norm_i8_vs_compiled_reference(H, gs, B, inplace):
+    rng = np.random.default_rng(H + B)
+    x = (rng.standard_normal((B, H)) * rng.uniform(0.1, 30)).astype(np.float32)
+    wq = rng.integers(-127, 128, H).astype(np.int8)
+    ws = rng.uniform(0.001, 0.02, H // gs).astype(np.float32)
+    np.testing.assert_array_equal(oracle.rms_norm_i8(x, wq, ws, gs, 1e-6, inplace),
+                                  oracle.ref_rms_norm_i8(x, wq, ws, gs, 1e-6, inplace))
+
+
+@ref
+def test_embedding_vs_compiled_reference():
+    rng = np.random.default_rng(2)
+    t = rng.integers(-127, 128, (100, 2048)).astype(np.int8)
+    s = rng.uniform(0.001, 0.02, 100).astype(np.float32)
+    np.testing.assert_array_equal(oracle.embedding_i8(t, s, 37), oracle.ref_embedding_i8(t, s, 37))
