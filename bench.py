@@ -1,5 +1,11 @@
 """Benchmark of the B200 INT8 hot path (one JSON line on rank 0).
 
+Headline: decode tokens/s of the Qwen3-VL-2B text decoder (28 layers, int8
+per-row weights, tied 151936-row LM head) at batch 1 per GPU (``--batch``),
+after a 452-token prompt (196 vision + 256 text tokens; its KV state is
+synthetic), one step = one generated token per request, 128 steps by default.
+The config-0 GEMV (below) is reported as ``gemv_config0``.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Workload: x fp32 [1,2048] ~N(0,1), W int8 [6144,2048]
@@ -156,6 +162,8 @@ def dist_env():
 
 
 def run_reference(args):
+    """The reference engine's own CPU operators (oracle/_ref) composed into
+    forward_text, timed on this host: `steps` decode tokens after warm-up."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
@@ -163,80 +171,198 @@ def run_reference(args):
     if not oracle.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqwen_ref.so not built"}))
         return
-    x, w, s = gemv_inputs(0)
-    cores = os.cpu_count()
-    for _ in range(args.warmup):
-        oracle.ref_i8_kernel(x, w, s, GEMV_K)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.ref_i8_kernel(x, w, s, GEMV_K)
-    dt = (time.perf_counter() - t0) / args.steps
-    gbs = GEMV_BYTES / dt / 1e9
+    tps, n, dt = cpu_decode_rate(args, seconds=None, steps=args.steps, warmup=args.warmup)
     print(json.dumps({
-        "impl": "reference", "metric": "int8_gemv_hbm_gbs", "value": round(gbs, 3), "unit": "GB/s",
+        "impl": "reference", "metric": "decode_tokens_per_s", "value": round(tps, 3), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32",
-        "data": "synthetic (seed 0)",
-        "config": {"workload": WORKLOAD, "l2": "CPU: one 12.6 MB weight copy, cache-warm"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
-                         "sample": f"{args.steps} calls of f32a_i8f32sb_f32c_avx2_kernel (OpenMP, all cores)"},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": "synthetic (random-init int8 weights, seed 0)", "config": decode_config(args, 1),
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                         "sample": f"{n} decode tokens, batch 1 (reference runs one request at a time)"},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
 
-def run_ours(args):
+PROMPT_CTX = 452          # 196 vision tokens + 256 text tokens
+
+
+def decode_config(args, ws):
+    return {"workload": f"qwen3vl2b_text_decode_b{args.batch}", "layers": 28, "hidden": 2048,
+            "intermediate": 6144, "heads": "16q/8kv x128", "vocab": 151936, "batch_per_gpu": args.batch,
+            "prompt_ctx": PROMPT_CTX, "weights": "int8 per-row scales, norms int8 group 128",
+            "parallelism": f"dp{ws} (independent replicas)", "l2": "1.72 GB of weights per step > L2"}
+
+
+_cpu_state = {}
+
+
+def cpu_decode_rate(args, seconds=None, steps=None, warmup=2):
+    """Reference CPU decode (compiled reference operators, all host cores) on
+    the same synthetic model; bounded by `seconds` or `steps`."""
     import torch
-    import torch.distributed as dist
+    import oracle
+    from oracle.decode import CpuDecoder
+    import_qvl()
+    import qvl_b200.decoder as D
+    cfg = D.TextConfig()
+    w = _cpu_state.get("w")
+    if w is None:
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        w = D.TextWeights.random(cfg, seed=0, device=dev).numpy()
+        _cpu_state["w"] = w
+    cos, sin = D.rope_table(PROMPT_CTX + 1024, cfg.head_dim, cfg.rope_theta)
+    backend = "ref" if oracle.ref_available() else "orc"
+    dec = CpuDecoder(cfg, w, PROMPT_CTX + 1024, cos, sin, backend=backend)
+    rng = np.random.default_rng(0)
+    dec.kc[:, :, :PROMPT_CTX] = rng.standard_normal((cfg.layers, cfg.kv_heads, PROMPT_CTX, cfg.head_dim),
+                                                    dtype=np.float32).astype(np.float16)
+    dec.vc[:, :, :PROMPT_CTX] = rng.standard_normal((cfg.layers, cfg.kv_heads, PROMPT_CTX, cfg.head_dim),
+                                                    dtype=np.float32).astype(np.float16)
+    tok, pos = 5, PROMPT_CTX
+    for _ in range(warmup):
+        _, tok = dec.step(tok, pos)
+        pos += 1
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _, tok = dec.step(tok, pos)
+        pos += 1
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (seconds is not None and el >= seconds):
+            break
+    dt = el / n
+    return 1.0 / dt, n, dt
+
+
+def run_gemv(dev, steps=640, warmup=5):
+    """BASELINE config 0 on this GPU: quantise + GEMV per step over rotated
+    weight copies (inputs > L2).  Returns device-timed GB/s of the step and of
+    the GEMV kernel alone."""
+    import torch
     qvl = import_qvl()
-    ws, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        dist.init_process_group("nccl", device_id=dev)
     x, w, s = gemv_inputs(0)
     xd = torch.from_numpy(x).to(dev)
     w0 = torch.from_numpy(w).to(dev)
     sd = torch.from_numpy(s).to(dev)
-    wc = [w0] + [w0.clone() for _ in range(N_COPIES - 1)]   # same values, distinct HBM
+    wc = [w0] + [w0.clone() for _ in range(N_COPIES - 1)]
     yd = torch.empty((1, GEMV_N), dtype=torch.float32, device=dev)
     work = qvl.Workspace(dev)
     work.get(qvl.load_library().qvl_linear_i8_workspace_bytes(1, GEMV_K, GEMV_K))
     q, qs = qvl.quantize_rows(xd, GEMV_K)
     stream = torch.cuda.Stream(dev)
-
-    def step(i):        # the product call: quantise + GEMV
-        qvl.linear(xd, wc[i % N_COPIES], sd, yd, group_quantized=False, workspace=work)
-
-    def kstep(i):       # the GEMV kernel alone (roofline timing)
-        qvl.linear_q16(q, qs, wc[i % N_COPIES], sd, GEMV_K, C=yd)
-
-    def capture(fn, n):
+    fns = {"step": lambda i: qvl.linear(xd, wc[i % N_COPIES], sd, yd, group_quantized=False, workspace=work),
+           "kernel": lambda i: qvl.linear_q16(q, qs, wc[i % N_COPIES], sd, GEMV_K, C=yd)}
+    out = {}
+    for name, fn in fns.items():
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             for i in range(3):
                 fn(i)
             torch.cuda.synchronize()
             with torch.cuda.graph(g, stream=stream):
-                for i in range(n):
+                for i in range(steps):
                     fn(i)
-        return g
+            for _ in range(warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        out[name] = GEMV_BYTES * steps / (e0.elapsed_time(e1) / 1e3) / 1e9
+    import oracle
+    if not np.array_equal(yd.cpu().numpy(), oracle.linear_i8(x, w, s, GEMV_K)):
+        raise SystemExit("bench: config-0 GEMV output differs from the oracle")
+    del wc
+    return {"workload": WORKLOAD, "step_gbs": round(out["step"], 1), "kernel_gbs": round(out["kernel"], 1),
+            "launches_per_step": 2, "steps": steps}
 
-    g_step = capture(step, args.steps)
-    g_kern = capture(kstep, args.steps)
-    torch.cuda.synchronize()
 
-    def timed(graph):
+def decode_gemv_roofline(dec, steps=4):
+    """Average GEMV launch of the decode step (q/k/v/o/gate/up/down x 28 +
+    LM head), timed alone in a graph: algorithmic bytes / device time."""
+    import torch
+    qvl = import_qvl()
+    cfg, t = dec.cfg, dec.w.t
+    B = dec.B
+    H, I = cfg.hidden, cfg.intermediate
+    q_h, s_h = qvl.quantize_rows(torch.randn(B, H, device=dec.device), H)
+    q_i, s_i = qvl.quantize_rows(torch.randn(B, I, device=dec.device), I)
+    outs = {n: torch.empty((B, t[n].shape[-2]), device=dec.device) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd")}
+    logits = torch.empty((B, cfg.vocab), device=dec.device)
+    nbytes = 0
+    calls = []
+    for l in range(cfg.layers):
+        for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+            W, S = t[n][l], t[n + "_s"][l]
+            qq, ss = (q_i, s_i) if n == "wd" else (q_h, s_h)
+            calls.append((qq, ss, W, S, outs[n]))
+            nbytes += W.numel() + 4 * W.shape[0] + B * (2 * W.shape[1] + 4 * W.shape[0])
+    calls.append((q_h, s_h, t["embed"], t["embed_s"], logits))
+    nbytes += t["embed"].numel() + 4 * cfg.vocab + B * (2 * H + 4 * cfg.vocab)
+    stream = torch.cuda.Stream(dec.device)
+    g = torch.cuda.CUDAGraph()
+    run = lambda: [qvl.linear_q16(a, b, c, d, a.shape[1], C=e, semantics=qvl.SEM_LANE8) for a, b, c, d, e in calls]
+    with torch.cuda.stream(stream):
+        run()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(steps):
+                run()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3
+    launches = len(calls) * steps * ((B + 7) // 8 if B > 4 else 1)
+    return nbytes * steps / sec / 1e9, nbytes / len(calls), sec / (len(calls) * steps), launches
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    qvl = import_qvl()
+    import qvl_b200.decoder as D
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = D.TextConfig()
+    B = args.batch
+    max_ctx = PROMPT_CTX + args.warmup + args.steps + 8
+    w = D.TextWeights.random(cfg, seed=rank, device=dev)
+    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev)
+    D.fill_kv_random(dec, PROMPT_CTX, seed=rank)
+    dec.tokens.copy_(torch.arange(B, dtype=torch.int32, device=dev) * 7919 % cfg.vocab)
+    stream = torch.cuda.Stream(dev)
+    # capture one decode token; replays advance positions on the device
+    with torch.cuda.stream(stream):
+        dec.step()                      # first call: kernel attribute set-up outside capture
+        torch.cuda.synchronize()
+        dec.positions.fill_(PROMPT_CTX)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dec.step()
+        torch.cuda.synchronize()
+        dec.positions.fill_(PROMPT_CTX)
+
+    def timed():
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
-                graph.replay()
+                g.replay()
             torch.cuda.synchronize()
             if ws > 1:
                 dist.barrier()
             torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            graph.replay()
+            for _ in range(args.steps):
+                g.replay()
             e1.record(stream)
             torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
@@ -247,71 +373,81 @@ def run_ours(args):
         return ms
 
     with ClockSampler(local) as clk:
-        ms_total = timed(g_step)
-        ms_kern = timed(g_kern)
-    ms_step = ms_total / args.steps
-    value = GEMV_BYTES * args.steps * ws / (ms_total / 1e3) / 1e9
+        ms = timed()
+    ms_step = ms / args.steps
+    value = B * ws * args.steps / (ms / 1e3)
+    # weights streamed per step + KV read per step (fp16, mean context)
+    w_bytes = sum(v.numel() * v.element_size() for v in w.t.values())
+    mean_ctx = PROMPT_CTX + args.warmup + args.steps / 2
+    kv_bytes = B * cfg.layers * 2 * cfg.kv_heads * cfg.head_dim * 2 * mean_ctx
+    step_gbs = (w_bytes + kv_bytes) / (ms_step / 1e3) / 1e9
 
-    # e2e through the public API with host buffers: pinned x -> device, linear,
-    # y -> pinned host; the host waits for each step's result.
-    xh = torch.from_numpy(x).pin_memory()
-    yh = torch.empty((1, GEMV_N), dtype=torch.float32).pin_memory()
-    graphs = []
-    for c in range(N_COPIES):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g, stream=stream):
-                xd.copy_(xh, non_blocking=True)
-                qvl.linear(xd, wc[c], sd, yd, group_quantized=False, workspace=work)
-                yh.copy_(yd, non_blocking=True)
-        graphs.append(g)
+    # e2e through the public API: pinned token ids -> device, one decode step,
+    # greedy ids -> pinned host; the host waits for every token.
+    tok_h = torch.zeros(B, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros(B, dtype=torch.int32).pin_memory()
+    dec.positions.fill_(PROMPT_CTX)
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            graphs[i % N_COPIES].replay()
+        ge = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ge, stream=stream):
+            dec.tokens.copy_(tok_h, non_blocking=True)
+            dec.step()
+            out_h.copy_(dec.tokens, non_blocking=True)
+        torch.cuda.synchronize()
+        dec.positions.fill_(PROMPT_CTX)
+        for _ in range(args.warmup):
+            ge.replay()
             stream.synchronize()
+            tok_h.copy_(out_h)
         if ws > 1:
             dist.barrier()
         t0 = time.perf_counter()
-        for i in range(args.steps):
-            graphs[i % N_COPIES].replay()
+        for _ in range(args.steps):
+            ge.replay()
             stream.synchronize()
+            tok_h.copy_(out_h)           # the host feeds back the generated ids
         e2e_s = time.perf_counter() - t0
     if ws > 1:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    y_check = yh.numpy().copy()
-    e2e = GEMV_BYTES * args.steps * ws / e2e_s / 1e9
+    e2e = B * ws * args.steps / e2e_s
 
+    gemv_gbs, gemv_bytes_per_launch, gemv_s_per_launch, _ = decode_gemv_roofline(dec)
+    lin_per_step = 7 * cfg.layers + 1
+    gemv_launch_mult = (B + 7) // 8 if B > 4 else 1
+    launches = args.steps * (1 + cfg.layers * 8 + 2 + lin_per_step * gemv_launch_mult)
+    gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
-        import oracle
-        if not np.array_equal(oracle.linear_i8(x, w, s, GEMV_K), y_check):
-            raise SystemExit("bench: GEMV output differs from the oracle")
         peak, peak_kind = load_peaks()
-        achieved = GEMV_BYTES / (ms_kern / args.steps / 1e3) / 1e9
         cpu = None
         if args.cpu_seconds > 0:
-            kind = "reference" if oracle.ref_available() else "port"
-            gbs, n, dt = cpu_gemv_rate(x, w, s, args.cpu_seconds, kind)
-            cpu = {"value": round(gbs, 3), "unit": "GB/s",
-                   "cores": os.cpu_count() if kind == "reference" else 1, "kind": kind,
-                   "sample": f"{n} GEMV calls ({dt * 1e3:.3f} ms each, weights cache-warm) over ~{args.cpu_seconds:.0f} s"}
+            del dec, g, ge
+            torch.cuda.empty_cache()
+            tps, n, dt = cpu_decode_rate(args, seconds=args.cpu_seconds)
+            import oracle
+            cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": os.cpu_count(),
+                   "kind": "reference" if oracle.ref_available() else "port",
+                   "sample": f"{n} decode tokens of one request ({dt * 1e3:.1f} ms each), same model shape, "
+                             f"reference operators compiled from its sources, OpenMP on all cores"}
         print(json.dumps({
-            "metric": "int8_gemv_hbm_gbs", "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+            "metric": "decode_tokens_per_s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int16xint8->int32", "data": "synthetic (seed 0)",
-            "config": {"workload": WORKLOAD, "parallelism": f"replicas{ws}",
-                       "l2": f"{N_COPIES} rotated weight copies ({N_COPIES * GEMV_N * GEMV_K / 1e6:.0f} MB > L2)"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profile_traffic("gemv_i8_config0"),
-                         "kernel": "gemv_i8_fast_kernel<1,true,4>", "algorithmic_bytes_per_launch": GEMV_BYTES},
-            "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": 4 * GEMV_K,
-                    "d2h_bytes_per_step": 4 * GEMV_N},
-            "gpu_launches": 2 * args.steps,
+            "dtype": "int16xint8->int32", "data": "synthetic (random-init int8 weights, seed = rank)",
+            "config": decode_config(args, ws),
+            "roofline": {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gemv_gbs / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profile_traffic("gemv_i8_config0"), "kernel": "gemv_i8 (decode GEMVs)",
+                         "algorithmic_bytes_per_launch": round(gemv_bytes_per_launch),
+                         "avg_launch_us": round(gemv_s_per_launch * 1e6, 3)},
+            "step_hbm_gbs": round(step_gbs, 1),
+            "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
+                    "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "gemv_config0": gemv0,
         }))
     if ws > 1:
         dist.destroy_process_group()
@@ -320,12 +456,15 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=640)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--batch", type=int, default=1, help="decode requests per GPU")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.cpu_seconds == 10.0:
+        args.cpu_seconds = 15.0
     if args.impl == "reference":
         run_reference(args)
     else:

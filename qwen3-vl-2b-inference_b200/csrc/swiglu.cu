@@ -27,45 +27,36 @@ __global__ void swiglu_kernel(float *__restrict gate, const float *__restrict up
         gate[i] = swiglu_one(gate[i], up[i]);
 }
 
-// One half-warp per K-group of the SwiGLU output row, as in
-// quantize_rows_kernel, with the SwiGLU value recomputed on the fly (it is
-// needed twice: for the sum of squares and for the quantisation).
-// grid: (ceil(G / 8), M); block 128.
-__global__ void __launch_bounds__(128)
+// grid: (ceil(G / gpb), M); block 256; gpb groups per block (<= 16, at most
+// 8192 values).  All threads compute the block's SwiGLU values into shared
+// memory, then each half-warp computes one group's scale (the reference's
+// sequential fused chain) and all threads quantise -- the arithmetic of
+// quantize_rows_kernel applied to swiglu(gate, up).
+__global__ void __launch_bounds__(256)
 swiglu_quant_kernel(const float *__restrict gate, const float *__restrict up,
-                    int16_t *__restrict q, float *__restrict s, int I, int g) {
+                    int16_t *__restrict q, float *__restrict s, int I, int g, int gpb) {
+    extern __shared__ __align__(16) float hs[];
+    __shared__ float inv_s[16];
     pdl_launch_dependents();
     pdl_wait();
     const int G = I / g;
-    int gi = blockIdx.x * 8 + (threadIdx.x >> 4);
+    const int g0 = blockIdx.x * gpb;
+    const int ng = min(gpb, G - g0);
     const int row = blockIdx.y;
-    const bool active = gi < G;
-    if (!active) gi = G - 1;
-    const int t16 = threadIdx.x & 15;
-    const size_t off = (size_t)row * I + (size_t)gi * g;
-    const float *gg = gate + off;
-    const float *uu = up + off;
-    const unsigned full = 0xffffffffu;
-    float acc = 0.0f;
-    for (int j = 0; j < g; j += 16) {
-        float v = swiglu_one(gg[j + t16], uu[j + t16]);
-        acc = fma_rn(v, v, acc);
+    const size_t base = (size_t)row * I + (size_t)g0 * g;
+    const int n = ng * g;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) hs[i] = swiglu_one(gate[base + i], up[base + i]);
+    __syncthreads();
+    const int hw = threadIdx.x >> 4;
+    const bool active = hw < ng;        // whole half-warps only: keep them in the shuffles
+    const int gl = active ? hw : 0;
+    const float sc = group_scale_ref(hs + (size_t)gl * g, g, threadIdx.x & 15);
+    if (active && (threadIdx.x & 15) == 0) {
+        s[(size_t)row * G + g0 + gl] = sc;
+        inv_s[gl] = __fdiv_rn(1.0f, sc);
     }
-    float o = __shfl_down_sync(full, acc, 8, 16);
-    float v = add_rn(acc, o);
-    o = __shfl_down_sync(full, v, 4, 16);
-    float u = add_rn(v, o);
-    o = __shfl_down_sync(full, u, 1, 16);
-    float p = add_rn(u, o);
-    o = __shfl_down_sync(full, p, 2, 16);
-    float ss = __shfl_sync(full, add_rn(p, o), 0, 16);
-    float inv_g = __fdiv_rn(1.0f, (float)g);
-    float rms = __fsqrt_rn(fma_rn(ss, inv_g, 1e-6f));
-    float sc = mul_rn(rms, inv127());
-    if (!active) return;
-    if (t16 == 0) s[(size_t)row * G + gi] = sc;
-    float inv = __fdiv_rn(1.0f, sc);
-    for (int j = t16; j < g; j += 16) q[off + j] = quant_one(swiglu_one(gg[j], uu[j]), inv);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) q[base + i] = quant_one(hs[i], inv_s[i / g]);
 }
 
 static void pdl_cfg(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStream_t stream) {
@@ -91,9 +82,17 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int16_t *q, 
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     pdl_cfg(cfg, attr, stream);
-    cfg.gridDim = dim3((I / g + 7) / 8, M);
-    cfg.blockDim = dim3(128);
-    return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, q, s, I, g);
+    int gpb = 8192 / g;
+    gpb = gpb < 1 ? 1 : (gpb > 16 ? 16 : gpb);
+    cfg.dynamicSmemBytes = (size_t)gpb * g * sizeof(float);
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)cfg.dynamicSmemBytes);
+        if (e != cudaSuccess) return e;
+    }
+    cfg.gridDim = dim3((I / g + gpb - 1) / gpb, M);
+    cfg.blockDim = dim3(256);
+    return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, q, s, I, g, gpb);
 }
 
 }  // namespace qvl
