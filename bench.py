@@ -414,9 +414,11 @@ def run_ours(args):
     e2e = B * ws * args.steps / e2e_s
 
     gemv_gbs, gemv_bytes_per_launch, gemv_s_per_launch, _ = decode_gemv_roofline(dec)
-    lin_per_step = 7 * cfg.layers + 1
-    gemv_launch_mult = (B + 7) // 8 if B > 4 else 1
-    launches = args.steps * (1 + cfg.layers * 8 + 2 + lin_per_step * gemv_launch_mult)
+    # per layer: rmsnorm, rope, 3 attention kernels, quantize, rmsnorm, swiglu-quant
+    # + GEMVs (q/k/v and gate/up share a launch when B <= 4; 8-row tiles above)
+    gemv_per_layer = 4 if B <= 4 else 7 * ((B + 7) // 8)
+    lm_head = 1 if B <= 4 else (B + 7) // 8
+    launches = args.steps * (1 + cfg.layers * (8 + gemv_per_layer) + 1 + lm_head + 1)
     gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = load_peaks()

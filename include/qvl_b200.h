@@ -94,6 +94,25 @@ int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
                       const float *B_scales, float *C, size_t M, size_t N, size_t K,
                       size_t group_size, int semantics, void *stream);
 
+/* Several products of the same activations in one launch (q/k/v from the
+ * normalised hidden state, or gate/up): C[i] = q . dequant(B[i])^T for
+ * i < n_mats <= 3, each B[i] int8 [N[i], K] with its own scales.  Host arrays
+ * of device pointers.  Results equal n_mats separate qvl_linear_q16_i8 calls. */
+int qvl_linear_q16_i8_multi(const int16_t *q, const float *q_scales, size_t n_mats,
+                            const int8_t *const *B, const float *const *B_scales, float *const *C,
+                            const size_t *N, size_t M, size_t K, size_t group_size, int semantics,
+                            void *stream);
+
+/* gate/up projections with SwiGLU in the epilogue (model/src/forward.cpp:
+ * 621-642): h[M, I] = swiglu(q . dequant(Wg)^T, q . dequant(Wu)^T) without
+ * writing gate or up.  One launch when M <= 4 and group_size >= 128; other
+ * shapes run the two products and swiglu separately and need up_scratch
+ * (fp32 [M, I]; nullable otherwise).  Values equal the unfused sequence. */
+int qvl_gate_up_swiglu_q16_i8(const int16_t *q, const float *q_scales, const int8_t *Wg,
+                              const float *sg, const int8_t *Wu, const float *su, float *h,
+                              float *up_scratch, size_t M, size_t I, size_t K, size_t group_size,
+                              int semantics, void *stream);
+
 /* ---- SwiGLU (layers/src/text_layer.cpp:420-434) ------------------------
  * gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i], in place, n elements. */
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);

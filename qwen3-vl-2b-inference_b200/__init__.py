@@ -43,7 +43,7 @@ EXPORTED = (
     "qvl_swiglu_mlp_workspace_bytes", "qvl_swiglu_mlp_i8", "qvl_rope_kv_append",
     "qvl_attention_workspace_bytes", "qvl_attention_decode", "qvl_argmax_rows",
     "qvl_qknorm_rope_kv_append", "qvl_rms_norm_i8", "qvl_embedding_lookup_i8",
-    "qvl_swiglu_quantize_rows",
+    "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -92,6 +92,8 @@ def load_library(path: str = LIB_PATH):
     L.qvl_rms_norm_i8.argtypes = [_P] * 6 + [_Z, _Z, _Z, ctypes.c_float, _I, _Z, _P]
     L.qvl_embedding_lookup_i8.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
     L.qvl_swiglu_quantize_rows.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
+    L.qvl_gate_up_swiglu_q16_i8.argtypes = [_P] * 8 + [_Z, _Z, _Z, _Z, _I, _P]
+    L.qvl_linear_q16_i8_multi.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _Z, _I, _P]
     _lib = L
     return L
 
@@ -297,3 +299,28 @@ def swiglu_quantize_rows(gate, up, q, q_scales, group_size, stream=None):
     _check(load_library().qvl_swiglu_quantize_rows(_ptr(gate), _ptr(up), _ptr(q), _ptr(q_scales), M, I,
                                                    group_size, _stream(stream)), "swiglu_quantize_rows")
     return q
+
+
+def linear_q16_multi(q, q_scales, mats, outs, group_size, semantics=SEM_REFERENCE, stream=None):
+    """outs[i] = q . dequant(mats[i])^T for up to three (W, scales) pairs in one launch."""
+    n = len(mats)
+    M, K = q.shape
+    Bp = (ctypes.c_void_p * n)(*[_ptr(w) for w, _ in mats])
+    Sp = (ctypes.c_void_p * n)(*[_ptr(s) for _, s in mats])
+    Cp = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    Np = (ctypes.c_size_t * n)(*[w.shape[0] for w, _ in mats])
+    _check(load_library().qvl_linear_q16_i8_multi(_ptr(q), _ptr(q_scales), n, Bp, Sp, Cp, Np, M, K,
+                                                  group_size, semantics, _stream(stream)), "linear_q16_multi")
+    return outs
+
+
+def gate_up_swiglu(q, q_scales, w_gate, s_gate, w_up, s_up, h, group_size, up_scratch=None,
+                   semantics=SEM_REFERENCE, stream=None):
+    """h = swiglu(gate(q), up(q)) with the SwiGLU fused into the GEMV epilogue."""
+    M, K = q.shape
+    I = w_gate.shape[0]
+    _check(load_library().qvl_gate_up_swiglu_q16_i8(_ptr(q), _ptr(q_scales), _ptr(w_gate), _ptr(s_gate),
+                                                    _ptr(w_up), _ptr(s_up), _ptr(h), _ptr(up_scratch), M, I,
+                                                    K, group_size, semantics, _stream(stream)),
+           "gate_up_swiglu")
+    return h

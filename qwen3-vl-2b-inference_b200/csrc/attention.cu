@@ -22,6 +22,8 @@
 #include <cfloat>
 #include "common.cuh"
 #include "attention.cuh"
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
 
 namespace qvl {
 
@@ -366,7 +368,202 @@ attn_combine_kernel(const int32_t *__restrict positions, int max_ctx, int chunk,
     o[dd] = mul_rn(a, inv);
 }
 
+// ---------------------------------------------------------------- cluster (one launch)
+// grid: (kClusterCtas, nq, NKV), cluster (kClusterCtas, 1, 1); block 256.
+// The kClusterCtas CTAs of a cluster own one (query, KV head) pair and split
+// its context into contiguous slices.  Each CTA keeps its raw scores in shared
+// memory; the CTAs exchange slice maxima, then slice sums and partial weighted
+// V sums, through distributed shared memory, and rank 0 writes the output.
+// The arithmetic is that of the split-K kernels (global max first, reference
+// exp polynomial, double-precision sum, zeroing rules) in a single launch
+// with no global scratch.
+constexpr int kClusterCtas = 8;
+constexpr int kSliceMax = 4096;          // tokens per CTA slice
+constexpr int kClusterThreads = 256;
+
+template <int KVM>
+__global__ void __launch_bounds__(kClusterThreads)
+attn_cluster_kernel(const float *__restrict q, const uint16_t *__restrict k_pages,
+                    const uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
+                    const int32_t *__restrict seq_ids, const int32_t *__restrict positions, int max_ctx,
+                    float *__restrict out, Dims d) {
+    extern __shared__ __align__(16) float sp[];          // [KVM][kSliceMax] scores / probabilities
+    __shared__ float accs[16][KVM][kD + 4];              // per token-lane partials, then [0] = CTA partial
+    __shared__ float redf[KVM][kClusterThreads / 32];
+    __shared__ double redd[KVM][kClusterThreads / 32];
+    __shared__ float lmax[KVM];
+    __shared__ double lsum[KVM];
+    __shared__ float gmax[KVM];
+    cg::cluster_group cluster = cg::this_cluster();
+    pdl_launch_dependents();
+    pdl_wait();
+    const int rank = (int)cluster.block_rank();
+    const int i = blockIdx.y, kvh = blockIdx.z;
+    const int ctx = min(positions[i] + 1, max_ctx);
+    const int per = (ctx + kClusterCtas - 1) / kClusterCtas;
+    const int t0 = min(ctx, rank * per), t1 = min(ctx, t0 + per);
+    const int len = t1 - t0;
+    const int32_t *pt_row = page_table + (size_t)seq_ids[i] * d.maxp;
+    const int t16 = threadIdx.x & 15, hw = threadIdx.x >> 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+    float qv[KVM][8];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) {
+        const float4 *qp = reinterpret_cast<const float4 *>(q + ((size_t)i * d.NH + kvh * KVM + h) * kD + t16 * 8);
+        float4 a = qp[0], b = qp[1];
+        qv[h][0] = a.x; qv[h][1] = a.y; qv[h][2] = a.z; qv[h][3] = a.w;
+        qv[h][4] = b.x; qv[h][5] = b.y; qv[h][6] = b.z; qv[h][7] = b.w;
+    }
+    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)kD));
+    const unsigned hmask = 0xffffu << (threadIdx.x & 16);
+    float mx[KVM];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) mx[h] = -INFINITY;
+    constexpr int U = 4;
+    for (int tb = hw; tb < len; tb += 16 * U) {
+        uint4 kr[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = tb + 16 * u;
+            kr[u] = (t < len) ? ld_stream_v4(kv_row(k_pages, pt_row, t0 + t, kvh, d) + t16) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = tb + 16 * u;
+            float kf[8];
+            h8_to_f8(kr[u], kf);
+#pragma unroll
+            for (int h = 0; h < KVM; ++h) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc = fma_rn(qv[h][e], kf[e], acc);
+#pragma unroll
+                for (int o = 8; o >= 1; o >>= 1) acc += __shfl_xor_sync(hmask, acc, o, 16);
+                const float sc = mul_rn(acc, inv_sqrt_d);
+                if (t < len) {
+                    mx[h] = fmaxf(mx[h], sc);
+                    if (t16 == 0) sp[h * kSliceMax + t] = sc;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) {
+        float m = mx[h];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) redf[h][warp] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x < KVM) {
+        float m = redf[threadIdx.x][0];
+        for (int w = 1; w < kClusterThreads / 32; ++w) m = fmaxf(m, redf[threadIdx.x][w]);
+        lmax[threadIdx.x] = m;
+    }
+    cluster.sync();                                       // slice maxima visible cluster-wide
+    if (threadIdx.x < KVM) {
+        float m = -INFINITY;
+        for (int r = 0; r < kClusterCtas; ++r) m = fmaxf(m, cluster.map_shared_rank(lmax, r)[threadIdx.x]);
+        gmax[threadIdx.x] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) {
+        const float M = gmax[h];
+        double part = 0.0;
+        for (int t = threadIdx.x; t < len; t += kClusterThreads) {
+            const float sv = sp[h * kSliceMax + t];
+            const float p = (sv > -INFINITY) ? exp_ref(sv - M) : 0.0f;
+            sp[h * kSliceMax + t] = p;
+            part += (double)p;
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0) redd[h][warp] = part;
+    }
+    __syncthreads();
+    if (threadIdx.x < KVM) {
+        double sum = 0.0;
+        for (int w = 0; w < kClusterThreads / 32; ++w) sum += redd[threadIdx.x][w];
+        lsum[threadIdx.x] = sum;
+    }
+    const int dg = t16, tl = hw;
+    float acc[KVM][8];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[h][e] = 0.0f;
+    for (int tb = tl; tb < len; tb += 16 * U) {
+        uint4 vr[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = tb + 16 * u;
+            vr[u] = (t < len) ? ld_stream_v4(kv_row(v_pages, pt_row, t0 + t, kvh, d) + dg) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = tb + 16 * u;
+            if (t < len) {
+                float vf[8];
+                h8_to_f8(vr[u], vf);
+#pragma unroll
+                for (int h = 0; h < KVM; ++h) {
+                    const float p = sp[h * kSliceMax + t];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[h][e] = fma_rn(p, vf[e], acc[h][e]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < KVM; ++h)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) accs[tl][h][dg * 8 + e] = acc[h][e];
+    __syncthreads();
+    float cpart[KVM];   // this CTA's partial for (h, dd) handled by this thread
+    for (int e = threadIdx.x; e < KVM * kD; e += kClusterThreads) {
+        const int h = e / kD, dd = e - h * kD;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 16; ++w) sum += accs[w][h][dd];
+        cpart[h] = sum;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < KVM * kD; e += kClusterThreads) {
+        const int h = e / kD, dd = e - h * kD;
+        accs[0][h][dd] = cpart[h];
+    }
+    cluster.sync();                                       // partial sums visible cluster-wide
+    if (rank == 0) {
+        for (int e = threadIdx.x; e < KVM * kD; e += kClusterThreads) {
+            const int h = e / kD, dd = e - h * kD;
+            double sum = 0.0;
+            float a = 0.0f;
+            for (int r = 0; r < kClusterCtas; ++r) {
+                sum += cluster.map_shared_rank(lsum, r)[h];
+                a += cluster.map_shared_rank(&accs[0][0][0], r)[h * (kD + 4) + dd];
+            }
+            const float M = gmax[h];
+            // the reference zeroes the row when the max is not finite or the
+            // sum is not a positive finite number (text_layer.cpp:466-469, :514-517)
+            const bool zero = ctx <= 0 || !isfinite(M) || !(sum > 0.0) || !isfinite(sum);
+            out[((size_t)i * d.NH + kvh * KVM + h) * kD + dd] = zero ? 0.0f : mul_rn(a, (float)(1.0 / sum));
+        }
+    }
+    cluster.sync();                                       // keep shared memory alive for rank 0's reads
+}
+
 // ---------------------------------------------------------------- host side
+// One cluster per (query, KV head) when every slice fits in shared memory
+// and the context is short enough that the cluster's CTAs are not starved,
+// or there are enough clusters to fill the GPU; split-K over the context
+// (three launches, global scratch) otherwise.
+bool attn_use_cluster(size_t nq, int max_ctx, int nkv) {
+    if (max_ctx > kClusterCtas * kSliceMax) return false;
+    return max_ctx <= 8192 || nq * (size_t)nkv * kClusterCtas >= 2 * 148;
+}
+
 int attn_chunk_tokens(size_t nq, int max_ctx, int nkv) {
     int chunk = kMaxChunk;
     while (chunk > 32 && (double)nq * nkv * ((max_ctx + chunk - 1) / chunk) < 2.0 * 148) chunk /= 2;
@@ -405,6 +602,29 @@ cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t stream, Args.
 template <int KVM>
 cudaError_t launch_attn_t(const AttnArgs &a, const AttnScratch &s, char *ws, cudaStream_t st) {
     Dims d{a.NH, a.NKV, a.P, a.maxp, a.max_pos};
+    if (attn_use_cluster(a.nq, a.max_ctx, a.NKV)) {
+        auto kern = attn_cluster_kernel<KVM>;
+        const size_t smem = (size_t)KVM * kSliceMax * sizeof(float);
+        // static + dynamic shared memory exceeds the 48 KB default: opt in
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kClusterCtas, (unsigned)a.nq, a.NKV);
+        cfg.blockDim = dim3(kClusterThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = kClusterCtas;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        return cudaLaunchKernelEx(&cfg, kern, a.q, a.k_pages, a.v_pages, a.page_table, a.seq_ids, a.positions,
+                                  a.max_ctx, a.out, d);
+    }
     float *scores = reinterpret_cast<float *>(ws + s.scores_off);
     float *cmax = reinterpret_cast<float *>(ws + s.cmax_off);
     float *psum = reinterpret_cast<float *>(ws + s.psum_off);

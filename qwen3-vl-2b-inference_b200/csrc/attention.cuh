@@ -42,6 +42,7 @@ struct AttnScratch {
     size_t scores_off, cmax_off, psum_off, pacc_off, total;
 };
 
+bool attn_use_cluster(size_t nq, int max_ctx, int nkv);
 int attn_chunk_tokens(size_t nq, int max_ctx, int nkv);
 AttnScratch attn_scratch_layout(size_t nq, int max_ctx, int NH, int nkv);
 cudaError_t launch_attention(const AttnArgs &a, void *workspace, cudaStream_t stream);

@@ -48,7 +48,7 @@ int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const flo
     if (mr == 0) return QVL_ERR_UNSUPPORTED;
     const size_t G = K / g;
     for (size_t m0 = 0; m0 < M; m0 += mr) {
-        qvl::GemvArgs a;
+        qvl::GemvArgs a = {};
         a.q = q + m0 * K;
         a.qs = qs + m0 * G;
         a.W = B;
@@ -139,6 +139,81 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     cudaStream_t st = (cudaStream_t)stream;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
     return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st, acc);
+}
+
+int qvl_linear_q16_i8_multi(const int16_t *q, const float *q_scales, size_t n_mats,
+                            const int8_t *const *B, const float *const *B_scales, float *const *C,
+                            const size_t *N, size_t M, size_t K, size_t group_size, int semantics,
+                            void *stream) {
+    if (!q || !q_scales || !B || !B_scales || !C || !N || n_mats == 0 || n_mats > 3) return QVL_ERR_INVALID;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    const int sem = semantics & ~QVL_SEM_ACCUMULATE;
+    if (sem < QVL_SEM_REFERENCE || sem > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    size_t total = 0;
+    for (size_t i = 0; i < n_mats; ++i) {
+        if (!B[i] || !B_scales[i] || !C[i] || !aligned(B[i], 16)) return QVL_ERR_INVALID;
+        int rc = check_linear_shape(M, N[i], K, group_size);
+        if (rc) return rc;
+        total += N[i];
+    }
+    if (!aligned(q, 16) || total > (size_t)INT32_MAX) return QVL_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    bool same_sem = true;
+    for (size_t i = 1; i < n_mats; ++i) same_sem &= lane8_for(sem, M, N[i], K) == lane8_for(sem, M, N[0], K);
+    if (qvl::gemv_fast_eligible((int)M, (int)K, (int)group_size) && same_sem) {
+        qvl::GemvArgs a = {};
+        a.q = q; a.qs = q_scales; a.M = (int)M; a.K = (int)K; a.g = (int)group_size; a.acc = acc;
+        size_t end = 0;
+        for (size_t i = 0; i < 3; ++i) {
+            if (i < n_mats) {
+                a.segs.W[i] = B[i]; a.segs.ws[i] = B_scales[i]; a.segs.y[i] = C[i]; a.segs.ldy[i] = (long)N[i];
+                end += N[i];
+            }
+            a.segs.end[i] = (int)end;
+        }
+        a.segs.nseg = (int)n_mats;
+        a.N = (int)total;
+        QVL_CUDA_TRY(qvl::launch_gemv_i8(a, lane8_for(sem, M, N[0], K), st));
+        return QVL_OK;
+    }
+    for (size_t i = 0; i < n_mats; ++i) {
+        int rc = run_q16_linear(q, q_scales, B[i], B_scales[i], C[i], M, N[i], K, group_size,
+                                lane8_for(sem, M, N[i], K), st, acc);
+        if (rc) return rc;
+    }
+    return QVL_OK;
+}
+
+int qvl_gate_up_swiglu_q16_i8(const int16_t *q, const float *q_scales, const int8_t *Wg,
+                              const float *sg, const int8_t *Wu, const float *su, float *h,
+                              float *up_scratch, size_t M, size_t I, size_t K, size_t group_size,
+                              int semantics, void *stream) {
+    if (!q || !q_scales || !Wg || !sg || !Wu || !su || !h) return QVL_ERR_INVALID;
+    if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    int rc = check_linear_shape(M, I, K, group_size);
+    if (rc) return rc;
+    if (!aligned(q, 16) || !aligned(Wg, 16) || !aligned(Wu, 16) || 2 * I > (size_t)INT32_MAX)
+        return QVL_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool lane8 = lane8_for(semantics, M, I, K);
+    if (qvl::gemv_fast_eligible((int)M, (int)K, (int)group_size)) {
+        qvl::GemvArgs a = {};
+        a.q = q; a.qs = q_scales; a.M = (int)M; a.K = (int)K; a.g = (int)group_size;
+        a.segs.W[0] = Wg; a.segs.ws[0] = sg; a.segs.y[0] = h; a.segs.ldy[0] = (long)I;
+        a.segs.W[1] = Wu; a.segs.ws[1] = su; a.segs.y[1] = h; a.segs.ldy[1] = (long)I;
+        a.segs.end[0] = (int)I; a.segs.end[1] = a.segs.end[2] = (int)(2 * I);
+        a.segs.nseg = 2;
+        a.N = (int)(2 * I);
+        a.pair = 1;
+        QVL_CUDA_TRY(qvl::launch_gemv_i8(a, lane8, st));
+        return QVL_OK;
+    }
+    if (!up_scratch) return QVL_ERR_WORKSPACE;
+    rc = run_q16_linear(q, q_scales, Wg, sg, h, M, I, K, group_size, lane8, st);
+    if (!rc) rc = run_q16_linear(q, q_scales, Wu, su, up_scratch, M, I, K, group_size, lane8, st);
+    if (rc) return rc;
+    QVL_CUDA_TRY(qvl::launch_swiglu(h, up_scratch, (long)(M * I), st));
+    return QVL_OK;
 }
 
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {

@@ -50,6 +50,16 @@ __device__ __forceinline__ float exp_ref(float x) {
     return mul_rn(y, p);
 }
 
+// SwiGLU of one element, layers/src/text_layer.cpp:430-432:
+// (x / (1 + expf(-x))) * u.  exp is evaluated in double precision and rounded
+// once to fp32 -- the correctly rounded expf value (glibc's expf, used by the
+// reference, is correctly rounded for all but a vanishing set of inputs).
+__device__ __forceinline__ float swiglu_one(float x, float u) {
+    float e = (float)exp(-(double)x);
+    float silu = __fdiv_rn(x, add_rn(1.0f, e));
+    return mul_rn(silu, u);
+}
+
 // 128-bit streaming load that bypasses L1 (weights are read exactly once).
 __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
     uint4 r;

@@ -38,9 +38,8 @@ constexpr int fast_min_blocks() { return (MR == 1 && IT <= 4) ? 6 : 1; }
 
 template <int MR, bool LANE, int IT>
 __global__ void __launch_bounds__(kThreads, fast_min_blocks<MR, IT>())
-gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
-                    const int8_t *__restrict W, const float *__restrict ws, float *__restrict y,
-                    int M, int N, int K, int g, long ldy, int acc, int seglog) {
+gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs, GemvSegs sg,
+                    int M, int N, int K, int g, int acc, int seglog, int pair) {
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *q_s = reinterpret_cast<int16_t *>(smem);
     const int G = K / g;
@@ -57,19 +56,27 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
     // occupancy there; otherwise the next row's loads are double-buffered.
     constexpr bool kDouble = IT <= 4 && MR > 1;
 
-    int n = blockIdx.x * kWarpsPerBlock + warp;
+    // pair = 1 (gate/up with SwiGLU epilogue): virtual rows 2p (segment 0,
+    // gate row p) and 2p+1 (segment 1, up row p) go to the same warp, one
+    // after the other, and the warp writes swiglu(gate, up) into segment 0.
+    const int wid = blockIdx.x * kWarpsPerBlock + warp;
+    int n = pair ? 2 * wid : wid;
+    auto next_row = [&](int r) { return pair ? ((r & 1) ? r - 1 + 2 * nwarps : r + 1) : r + nwarps; };
     uint4 wr[IT];
     float wsr[2];
     auto issue = [&](int row, uint4 *dst, float *sdst) {
-        const uint4 *base = reinterpret_cast<const uint4 *>(W + (long)row * K) + lane;
+        const int sid = pair ? (row & 1) : sg.seg_of(row);
+        const int lr = pair ? (row >> 1) : row - sg.start(sid);
+        const int8_t *W = sg.w_of(sid);
+        const float *ws = sg.ws_of(sid) + (long)lr * G;
+        const uint4 *base = reinterpret_cast<const uint4 *>(W + (long)lr * K) + lane;
 #pragma unroll
         for (int it = 0; it < IT; ++it) {
             const int c = it * 32 + lane;
             dst[it] = (c < NCH) ? ld_stream_v4(base + it * 32) : make_uint4(0, 0, 0, 0);
         }
-        const float *wsrow = ws + (long)row * G;
-        sdst[0] = (lane < G) ? __ldg(wsrow + lane) : 0.0f;
-        sdst[1] = (lane + 32 < G) ? __ldg(wsrow + lane + 32) : 0.0f;
+        sdst[0] = (lane < G) ? __ldg(ws + lane) : 0.0f;
+        sdst[1] = (lane + 32 < G) ? __ldg(ws + lane + 32) : 0.0f;
     };
     if (n < N) issue(n, wr, wsr);
 
@@ -88,10 +95,11 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
     const int pos = lane & (seg - 1);
     const int d1 = seg >> 1, d2 = seg >> 2, d3 = seg >> 3;   // transposing-butterfly distances
 
-    for (; n < N; n += nwarps) {
+    float gate_v[MR];
+    for (; n < N; n = next_row(n)) {
         uint4 nx[kDouble ? IT : 1];
         float nws[2] = {0.0f, 0.0f};
-        const int nn = n + nwarps;
+        const int nn = next_row(n);
         if constexpr (kDouble) {
             if (nn < N) issue(nn, nx, nws);
         }
@@ -185,8 +193,15 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs,
                 float p = add_rn(u, __shfl_xor_sync(full, u, d3));
                 out = add_rn(p, __shfl_xor_sync(full, p, d2));
             }
-            if (lane == 0) {
-                float *yp = y + (long)m * ldy + n;
+            if (pair) {
+                if ((n & 1) == 0) {
+                    gate_v[m] = out;
+                } else if (lane == 0) {
+                    sg.y[0][(long)m * sg.ldy[0] + (n >> 1)] = swiglu_one(gate_v[m], out);
+                }
+            } else if (lane == 0) {
+                const int sid = sg.seg_of(n);
+                float *yp = sg.y_of(sid) + (long)m * sg.ldy_of(sid) + (n - sg.start(sid));
                 *yp = acc ? add_rn(*yp, out) : out;   // residual add: add_vector order
             }
         }
@@ -216,7 +231,8 @@ cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (per_sm < 1) per_sm = 1;
-    long want = (a.N + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    const long total_rows = a.segs.nseg ? a.segs.total() : a.N;
+    long want = (total_rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
     long cap = (long)sms * per_sm;
     int grid = (int)(want < cap ? want : cap);
     const int cpg = a.g / 16;
@@ -232,8 +248,9 @@ cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, a.W, a.ws, a.y, a.M, a.N, a.K, a.g, a.ldy, a.acc,
-                              seglog);
+    GemvSegs sg = a.segs;
+    if (sg.nseg == 0) sg = GemvSegs::single(a.W, a.ws, a.y, a.N, a.ldy);
+    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, sg, a.M, sg.total(), a.K, a.g, a.acc, seglog, a.pair);
 }
 
 template <int MR, bool LANE>

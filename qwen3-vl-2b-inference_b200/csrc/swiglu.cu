@@ -14,11 +14,6 @@
 
 namespace qvl {
 
-__device__ __forceinline__ float swiglu_one(float x, float u) {
-    float e = (float)exp(-(double)x);
-    float silu = __fdiv_rn(x, add_rn(1.0f, e));
-    return mul_rn(silu, u);
-}
 
 __global__ void swiglu_kernel(float *__restrict gate, const float *__restrict up, long n) {
     pdl_launch_dependents();

@@ -29,7 +29,8 @@ import numpy as np
 import torch
 
 from . import (SEM_ACCUMULATE, SEM_LANE8, PagedKV, Workspace, attention, embedding_lookup_i8,
-               greedy_decode, linear_q16, qknorm_rope_kv_append, rms_norm_i8, swiglu_quantize_rows)
+               gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, qknorm_rope_kv_append,
+               rms_norm_i8)
 from . import load_library
 
 
@@ -149,6 +150,11 @@ class TextDecoder:
         S = t[name + "_s"][l] if l is not None else t[name + "_s"]
         return linear_q16(q, qs, W, S, q.shape[1], C=out, semantics=SEM_LANE8 | (SEM_ACCUMULATE if acc else 0))
 
+    def _lin_multi(self, q, qs, names, l, outs):
+        t = self.w.t
+        mats = [(t[n][l], t[n + "_s"][l]) for n in names]
+        return linear_q16_multi(q, qs, mats, outs, q.shape[1], semantics=SEM_LANE8)
+
     def step(self, B=None):
         """One decode token for requests 0..B-1: reads self.tokens and
         self.positions, leaves the logits in self.logits and the greedy
@@ -163,9 +169,7 @@ class TextDecoder:
         embedding_lookup_i8(t["embed"], t["embed_s"], self.tokens[:B], x)
         for l in range(cfg.layers):
             rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
-            self._lin(qx, qx_s, "wq", l, self.q[:B])
-            self._lin(qx, qx_s, "wk", l, self.k[:B])
-            self._lin(qx, qx_s, "wv", l, self.v[:B])
+            self._lin_multi(qx, qx_s, ("wq", "wk", "wv"), l, (self.q[:B], self.k[:B], self.v[:B]))
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
@@ -173,9 +177,9 @@ class TextDecoder:
             _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
             self._lin(self.qa[:B], self.qa_s[:B], "wo", l, x, acc=True)
             rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
-            self._lin(qx, qx_s, "wg", l, self.gate[:B])
-            self._lin(qx, qx_s, "wu", l, self.up[:B])
-            swiglu_quantize_rows(self.gate[:B], self.up[:B], self.qh[:B], self.qh_s[:B], cfg.intermediate)
+            gate_up_swiglu(qx, qx_s, t["wg"][l], t["wg_s"][l], t["wu"][l], t["wu_s"][l], self.gate[:B], H,
+                           up_scratch=self.up[:B], semantics=SEM_LANE8)
+            _quantize_into(self.gate[:B], self.qh[:B], self.qh_s[:B])
             self._lin(self.qh[:B], self.qh_s[:B], "wd", l, x, acc=True)
         rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s, quant_group=H,
                     inplace_form=True)
@@ -185,7 +189,7 @@ class TextDecoder:
 
     # launches of our kernels per step (attention = 3 kernels)
     def kernels_per_step(self):
-        return 1 + self.cfg.layers * (1 + 3 + 1 + 3 + 1 + 1 + 1 + 2 + 1 + 1) + 1 + 1 + 1
+        return 1 + self.cfg.layers * (1 + 1 + 1 + 3 + 1 + 1 + 1 + 1 + 1 + 1) + 1 + 1 + 1
 
 
 def _quantize_into(x, q, qs):
