@@ -440,7 +440,7 @@ def run_ours(args):
             "config": decode_config(args, ws),
             "roofline": {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gemv_gbs / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profile_traffic("gemv_i8_config0"), "kernel": "gemv_i8 (decode GEMVs)",
+                         "traffic": profile_traffic("gemv_i8_decode"), "kernel": "gemv_i8 (decode GEMVs)",
                          "algorithmic_bytes_per_launch": round(gemv_bytes_per_launch),
                          "avg_launch_us": round(gemv_s_per_launch * 1e6, 3)},
             "step_hbm_gbs": round(step_gbs, 1),
