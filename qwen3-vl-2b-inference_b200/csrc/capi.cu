@@ -38,10 +38,15 @@ bool lane8_for(int semantics, size_t M, size_t N, size_t K) {
 
 // y[M,N] from pre-quantised activations: CUDA-core GEMV for small M (and for
 // the LANE8 summation order at any M), tensor cores for TILED at M >= 16.
+// tc_planes: workspace for the tensor-core path's hi/lo activation planes
+// (gemm_tc_planes_bytes); nullptr keeps the product on the CUDA-core GEMV.
 int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const float *Bs, float *C,
-                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st, int acc = 0) {
-    if (!lane8 && !acc && qvl::gemm_tc_supported(M, N, K, g)) {
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, B, Bs, C, (int)M, (int)N, (int)K, (int)g, st));
+                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st, int acc = 0,
+                   void *tc_planes = nullptr) {
+    if (tc_planes && !lane8 && !acc && qvl::gemm_tc_supported(M, N, K, g)) {
+        int8_t *hi = static_cast<int8_t *>(tc_planes);
+        uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, K) / 2;
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, hi, lo, B, Bs, C, (int)M, (int)N, (int)K, st));
         return QVL_OK;
     }
     const int mr = gemv_rows_per_launch(K, g);
@@ -104,7 +109,9 @@ int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, siz
 
 size_t qvl_linear_i8_workspace_bytes(size_t M, size_t K, size_t group_size) {
     if (group_size == 0 || K % group_size) return 0;
-    return qbuf_bytes(M, K, group_size);
+    size_t b = qbuf_bytes(M, K, group_size);
+    if (M >= 16 && group_size == K && K % 128 == 0) b += qvl::gemm_tc_planes_bytes(M, K);
+    return b;
 }
 
 int qvl_linear_q16_i8(const int16_t *q, const float *q_scales, const int8_t *B,
@@ -138,7 +145,11 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     float *qs = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * K * 2));
     cudaStream_t st = (cudaStream_t)stream;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
-    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st, acc);
+    void *planes = nullptr;
+    if (M >= 16 && g == K && K % 128 == 0 &&
+        workspace_bytes >= need + qvl::gemm_tc_planes_bytes(M, K))
+        planes = static_cast<char *>(workspace) + need;
+    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st, acc, planes);
 }
 
 int qvl_linear_q16_i8_multi(const int16_t *q, const float *q_scales, size_t n_mats,

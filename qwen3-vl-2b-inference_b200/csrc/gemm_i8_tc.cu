@@ -1,10 +1,267 @@
-#include "common.cuh"
+// INT8 GEMM on the 5th-generation tensor cores (tcgen05, kind::i8) for
+// prefill-shaped products: C[M, N] = A[M, K] . dequant(W[N, K])^T with the
+// reference's TILED summation (matmul/src/cpu_f32a_i8f32sb_f32c_avx2.cpp:
+// 538-653) and per-output-row weight scales (group = K).
+//
+// Exactness.  The reference multiplies int16 activations by int8 weights.
+// int16 does not fit an int8 MMA operand, so each quantised activation is
+// split exactly as q = 256*hi + lo with hi = q >> 8 (signed 8-bit) and
+// lo = q & 255 (unsigned 8-bit).  Two MMAs per K step accumulate
+// D_hi = W.hi and D_lo = W.lo in int32 in tensor memory, and the epilogue
+// forms S = 256*D_hi + D_lo, the exact integer dot product (|S| < 2^31 for
+// any quantised row).  The fp32 epilogue is the reference's:
+// C = fma(float(S) * a_s, w_s, 0).
+//
+// Tiling.  "Swap AB": the MMA's M dimension is 128 weight rows (TMEM lanes),
+// its N dimension a tile of NT activation rows (TMEM columns), K steps of 32
+// bytes.  A CTA computes a 128 x NT tile; one thread issues the TMA loads of
+// a 4-stage ring (128 B of K per stage, 128-byte swizzle), another thread
+// issues the MMAs and commits each stage back to the ring, and four warps
+// read the accumulators (tcgen05.ld) for the epilogue.  Every wait is bounded.
+#include <cstdio>
+#include <mutex>
+#include "tc_common.cuh"
 #include "gemm_i8_tc.cuh"
 
 namespace qvl {
-bool gemm_tc_supported(size_t, size_t, size_t, size_t) { return false; }
-cudaError_t launch_gemm_i8_tc(const int16_t *, const float *, const int8_t *, const float *, float *,
-                              int, int, int, int, cudaStream_t) {
-    return cudaErrorNotSupported;
+
+namespace {
+constexpr int kBM = 128;          // weight rows per CTA (MMA M)
+constexpr int kBK = 128;          // bytes of K per stage
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr int kUmmaK = 32;        // K per kind::i8 MMA
+}  // namespace
+
+__device__ int g_gemm_tc_timeout = 0;
+
+template <int NT>
+struct TcSmem {
+    static constexpr int kA = kBM * kBK;          // 16 KB
+    static constexpr int kB = NT * kBK;           // one activation plane
+    static constexpr int kStage = kA + 2 * kB;
+    static constexpr int kBytes = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+};
+
+// grid: (ceil(N/128), ceil(M/NT)); block 128.
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
+                  const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
+                  const float *__restrict w_scale, float *__restrict C, int M, int N, int K) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    using L = TcSmem<NT>;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * L::kStage);
+    const uint32_t full0 = tc::smem_u32(bars);                 // [kStages]
+    const uint32_t empty0 = tc::smem_u32(bars + kStages);      // [kStages]
+    const uint32_t accbar = tc::smem_u32(bars + 2 * kStages);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kBM;
+    const int m0 = blockIdx.y * NT;
+    const int nk = K / kBK;
+    constexpr uint32_t kCols = (2 * NT < 32) ? 32 : 2 * NT;   // power of two >= 32
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(full0 + 8 * s, 1);
+            tc::mbar_init(empty0 + 8 * s, 1);
+        }
+        tc::mbar_init(accbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        tc::prefetch_tmap(&tm_w);
+        tc::prefetch_tmap(&tm_hi);
+        tc::prefetch_tmap(&tm_lo);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t d_hi = tmem, d_lo = tmem + NT;
+
+    pdl_launch_dependents();
+    bool ok = true;
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer (weights first: they do not depend on the previous kernel)
+        for (int kb = 0; kb < nk && ok; ++kb) {
+            const int s = kb % kStages;
+            if (kb >= kStages) ok = tc::mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, &g_gemm_tc_timeout);
+            if (!ok) break;
+            unsigned char *st = smem + s * L::kStage;
+            tc::mbar_expect_tx(full0 + 8 * s, L::kStage);
+            tc::tma_load_2d(tc::smem_u32(st), &tm_w, kb * kBK, n0, full0 + 8 * s);
+            if (kb == 0) pdl_wait();   // activations come from the previous kernel
+            tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, kb * kBK, m0, full0 + 8 * s);
+            tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, kb * kBK, m0, full0 + 8 * s);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t id_hi = tc::idesc_i8(kBM, NT, true);
+        constexpr uint32_t id_lo = tc::idesc_i8(kBM, NT, false);
+        for (int kb = 0; kb < nk && ok; ++kb) {
+            const int s = kb % kStages;
+            ok = tc::mbar_wait(full0 + 8 * s, (kb / kStages) & 1, &g_gemm_tc_timeout);
+            if (!ok) break;
+            tc::tc_fence_after();
+            const uint32_t a_base = tc::smem_u32(smem + s * L::kStage);
+            const uint32_t h_base = a_base + L::kA;
+            const uint32_t l_base = h_base + L::kB;
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+                const uint64_t ad = tc::sdesc_k_sw128(a_base + k * kUmmaK);
+                const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                tc::mma_i8(d_hi, ad, tc::sdesc_k_sw128(h_base + k * kUmmaK), id_hi, acc);
+                tc::mma_i8(d_lo, ad, tc::sdesc_k_sw128(l_base + k * kUmmaK), id_lo, acc);
+            }
+            tc::tc_commit(empty0 + 8 * s);   // frees the stage once these MMAs have read it
+        }
+        tc::tc_commit(accbar);               // accumulators complete
+    }
+    __syncwarp();
+
+    // ---- epilogue: 4 warps, warp w owns TMEM lanes (weight rows) 32w..32w+31
+    pdl_wait();   // activation scales and C belong to the stream order
+    const bool acc_ok = tc::mbar_wait(accbar, 0, &g_gemm_tc_timeout);
+    tc::tc_fence_after();
+    if (acc_ok) {
+        const int n = n0 + warp * 32 + lane;
+        const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+#pragma unroll 1
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            uint32_t hi[16], lo[16];
+            tc::tmem_ld16(d_hi + lane_off + c0, hi);
+            tc::tmem_ld16(d_lo + lane_off + c0, lo);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int m = m0 + c0 + j;
+                if (m < M && n < N) {
+                    const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
+                    const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
+                    C[(size_t)m * N + n] = fma_rn(p, ws, 0.0f);
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, kCols);
 }
+
+// q int16 [M, K] -> hi int8 [M, K] (q >> 8), lo uint8 [M, K] (q & 255).
+__global__ void split_hi_lo_kernel(const int16_t *__restrict q, int8_t *__restrict hi, uint8_t *__restrict lo,
+                                   long n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n / 8; i += (long)gridDim.x * blockDim.x) {
+        const int4 v = reinterpret_cast<const int4 *>(q)[i];
+        const int16_t *e = reinterpret_cast<const int16_t *>(&v);
+        uint2 h, l;
+        unsigned char *hb = reinterpret_cast<unsigned char *>(&h);
+        unsigned char *lb = reinterpret_cast<unsigned char *>(&l);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            hb[j] = (unsigned char)(e[j] >> 8);
+            lb[j] = (unsigned char)(e[j] & 255);
+        }
+        reinterpret_cast<uint2 *>(hi)[i] = h;
+        reinterpret_cast<uint2 *>(lo)[i] = l;
+    }
+}
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled get_encode() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// 2-D uint8 tensor [rows, cols] (cols contiguous), box {128 bytes, box_rows}, 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    EncodeTiled enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NT>
+cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
+                      const float *ws, float *C, int M, int N, int K, cudaStream_t st) {
+    auto kern = gemm_i8_tc_kernel<NT>;
+    const int smem = TcSmem<NT>::kBytes;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((N + kBM - 1) / kBM, (M + NT - 1) / NT);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K);
+}
+
+}  // namespace
+
+bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
+    return M >= 16 && g == K && K % kBK == 0 && N >= kBM && get_encode() != nullptr;
+}
+
+size_t gemm_tc_planes_bytes(size_t M, size_t K) { return 2 * ((M * K + 255) & ~(size_t)255); }
+
+cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,
+                              const float *ws, float *C, int M, int N, int K, cudaStream_t stream) {
+    {
+        cudaLaunchConfig_t cfg = {};
+        const long n = (long)M * K;
+        long blocks = (n / 8 + 255) / 256;
+        cfg.gridDim = dim3((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8));
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, split_hi_lo_kernel, q, hi, lo, n);
+        if (e != cudaSuccess) return e;
+    }
+    const int NT = M >= 1024 ? 128 : (M >= 64 ? 64 : 32);
+    CUtensorMap mw, mh, ml;
+    if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
+        return cudaErrorInvalidValue;
+    if (NT == 128) return launch_nt<128>(mw, mh, ml, qs, ws, C, M, N, K, stream);
+    if (NT == 64) return launch_nt<64>(mw, mh, ml, qs, ws, C, M, N, K, stream);
+    return launch_nt<32>(mw, mh, ml, qs, ws, C, M, N, K, stream);
+}
+
 }  // namespace qvl

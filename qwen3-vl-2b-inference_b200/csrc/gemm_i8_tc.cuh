@@ -5,7 +5,10 @@
 
 namespace qvl {
 // Tensor-core (tcgen05 kind::i8) INT8 GEMM with TILED summation semantics.
+// TILED summation, per-output-row weight scales (g == K), K % 128 == 0, M >= 16.
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g);
-cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, const int8_t *W, const float *ws,
-                              float *C, int M, int N, int K, int g, cudaStream_t stream);
+// bytes of the hi/lo activation planes the GEMM needs in the caller's workspace
+size_t gemm_tc_planes_bytes(size_t M, size_t K);
+cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,
+                              const float *ws, float *C, int M, int N, int K, cudaStream_t stream);
 }  // namespace qvl

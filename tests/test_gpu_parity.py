@@ -229,3 +229,21 @@ def test_argmax_tie_and_nan(qvl, cuda):
     x[2, :] = -np.inf
     idx = qvl.greedy_decode(dev(x, cuda)).cpu().numpy()
     assert list(idx) == [oracle.argmax(r) for r in x] == [7, 2, 0]
+
+
+# ------------------------------------------------------------ tensor-core GEMM
+@pytest.mark.parametrize("M,N,K", [(16, 128, 128), (512, 2048, 2048), (512, 1024, 2048), (512, 6144, 2048),
+                                   (512, 2048, 6144), (130, 2048, 2048), (2048, 256, 2048), (77, 300, 1024)])
+def test_linear_prefill_tensor_core_bit_exact(qvl, cuda, M, N, K):
+    """M >= 16 with per-row scales runs the tcgen05 kind::i8 GEMM (hi/lo split
+    of the int16 activations); TILED order, bit-exact with the oracle."""
+    x, w, ws = make_linear_inputs(7 * M + N, M, N, K, K)
+    y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=False)
+    np.testing.assert_array_equal(y.cpu().numpy(), oracle.linear_i8(x, w, ws, K, oracle.TILED))
+
+
+def test_linear_prefill_lm_head_rows(qvl, cuda):
+    x, w, ws = make_linear_inputs(3, 64, 151936, 2048, 2048)
+    y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=False).cpu().numpy()
+    ref = oracle.linear_i8(x[:4], w, ws, 2048, oracle.TILED)
+    np.testing.assert_array_equal(y[:4], ref)
