@@ -322,6 +322,81 @@ def decode_gemv_roofline(dec, steps=4):
     return nbytes * steps / sec / 1e9, nbytes / len(calls), sec / (len(calls) * steps), launches
 
 
+PREFILL_SHAPES = [(2048, 2048), (1024, 2048), (6144, 2048), (2048, 6144), (151936, 2048)]   # (N, K), config 1
+
+
+def run_prefill_gemm(args):
+    """batched INT8 GEMM at M=512 over the q/o, k/v,
+    gate/up, down and LM-head shapes (per-row scales), one pass over all five
+    shapes per step, through qvl.linear (quantise + hi/lo split + tcgen05)."""
+    import torch
+    import torch.distributed as dist
+    qvl = import_qvl()
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    M = args.m
+    g = torch.Generator(device=dev).manual_seed(rank)
+    mats = []
+    for N, K in PREFILL_SHAPES:
+        W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        S = torch.rand(N, device=dev, generator=g) * 0.019 + 0.001
+        X = torch.randn(M, K, device=dev, generator=g)
+        Y = torch.empty(M, N, device=dev)
+        mats.append((X, W, S, Y))
+    work = qvl.Workspace(dev)
+    work.get(max(qvl.load_library().qvl_linear_i8_workspace_bytes(M, K, K) for _, K in PREFILL_SHAPES))
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for X, W, S, Y in mats:
+            qvl.linear(X, W, S, Y, group_quantized=False, workspace=work)
+
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step()
+        for _ in range(args.warmup):
+            gr.replay()
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                gr.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ops = sum(2 * M * N * K for N, K in PREFILL_SHAPES)
+    tops = ops * args.steps * ws / (ms / 1e3) / 1e12
+    if rank == 0:
+        import oracle
+        X, W, S, Y = mats[0]
+        ref = oracle.linear_i8(X[:2].cpu().numpy(), W.cpu().numpy(), S.cpu().numpy(), 2048, oracle.TILED)
+        if not np.array_equal(Y[:2].cpu().numpy(), ref):
+            raise SystemExit("bench: prefill GEMM differs from the oracle")
+        print(json.dumps({
+            "metric": "int8_prefill_gemm_tops", "value": round(tops, 2), "unit": "TOPS", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic",
+            "config": {"workload": f"config1_gemm_M{M}", "shapes_NK": PREFILL_SHAPES,
+                       "ops_per_step": ops, "note": "ops = 2*M*N*K (the hi/lo split doubles the MMA work)"},
+            "clocks": clk.summary(), "gpu_launches": 3 * len(PREFILL_SHAPES) * args.steps,
+        }))
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -463,12 +538,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill_gemm"])
+    ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.cpu_seconds == 10.0:
         args.cpu_seconds = 15.0
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill_gemm":
+        run_prefill_gemm(args)
     else:
         run_ours(args)
 

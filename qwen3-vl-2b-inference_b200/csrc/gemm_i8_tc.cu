@@ -255,7 +255,7 @@ cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uin
         cudaError_t e = cudaLaunchKernelEx(&cfg, split_hi_lo_kernel, q, hi, lo, n);
         if (e != cudaSuccess) return e;
     }
-    const int NT = M >= 1024 ? 128 : (M >= 64 ? 64 : 32);
+    const int NT = M >= 256 ? 128 : (M >= 64 ? 64 : 32);
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
