@@ -489,11 +489,20 @@ def run_ours(args):
     e2e = B * ws * args.steps / e2e_s
 
     gemv_gbs, gemv_bytes_per_launch, gemv_s_per_launch, _ = decode_gemv_roofline(dec)
-    # per layer: rmsnorm, rope, 3 attention kernels, quantize, rmsnorm, swiglu-quant
-    # + GEMVs (q/k/v and gate/up share a launch when B <= 4; 8-row tiles above)
-    gemv_per_layer = 4 if B <= 4 else 7 * ((B + 7) // 8)
-    lm_head = 1 if B <= 4 else (B + 7) // 8
-    launches = args.steps * (1 + cfg.layers * (8 + gemv_per_layer) + 1 + lm_head + 1)
+    lib = qvl.load_library()
+    tc_mode = dec.use_tc
+    attn_k = 1 if max_ctx <= 8192 else 3          # cluster kernel / split-K trio
+    if dec.use_tc:   # rmsnorm, split+3 GEMMs, rope, attention, quantize, split+GEMM, rmsnorm,
+        # split+2 GEMMs+swiglu, quantize, split+GEMM
+        per_layer, head = 1 + 4 + 1 + attn_k + 1 + 2 + 1 + 4 + 1 + 2, 1 + 1 + 2 + 1
+    elif B == 1:  # qkv, rope, attention, quantize, o(+norm tail), gate/up(+quant tail), down(+norm tail)
+        per_layer, head = 6 + attn_k, 1 + 1 + 1 + 1  # embedding, first rmsnorm, LM head, argmax
+    elif B <= 4:  # fast GEMV without the fused tails
+        per_layer, head = 9 + attn_k, 1 + 2 + 1
+    else:        # 8-row GEMV tiles, separate norms / swiglu
+        tiles = (B + 7) // 8
+        per_layer, head = 5 + attn_k + 7 * tiles, 1 + 1 + tiles + 1
+    launches = args.steps * (cfg.layers * per_layer + head)
     gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = load_peaks()
@@ -512,7 +521,9 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int16xint8->int32", "data": "synthetic (random-init int8 weights, seed = rank)",
-            "config": decode_config(args, ws),
+            "config": dict(decode_config(args, ws),
+                           batch_order="tiled (M=B tcgen05, reference M>1 order)" if tc_mode
+                           else "lane8 (each request in the reference M=1 order)"),
             "roofline": {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gemv_gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": profile_traffic("gemv_i8_decode"), "kernel": "gemv_i8 (decode GEMVs)",

@@ -113,6 +113,48 @@ int qvl_gate_up_swiglu_q16_i8(const int16_t *q, const float *q_scales, const int
                               float *up_scratch, size_t M, size_t I, size_t K, size_t group_size,
                               int semantics, void *stream);
 
+/* Fused tail of a product: after the last output of the launch is written,
+ * the row(s) of C[0] (length N[0]) are RMS-normalised (norm_w != NULL;
+ * qvl_rms_norm_i8 arithmetic) and/or quantised for the next linear --
+ * e.g. o_proj + residual -> post-attention rms_norm -> gate/up input, or
+ * down_proj + residual -> next layer's input rms_norm -> q/k/v input.
+ * `counter` is a device int that must be 0 before the first call; each call
+ * leaves it 0 again (calls that overlap on the GPU need distinct counters). */
+typedef struct {
+    int *counter;
+    const int8_t *norm_w;     /* NULL: quantise C[0] as is */
+    const float *norm_s;
+    size_t norm_group;
+    float eps;
+    int inplace_form;         /* 1: rms_norm_inplace rounding */
+    float *norm_out;          /* normalised copy of C[0] (nullable, may alias C[0]) */
+    int16_t *q;               /* quantised activations for the next linear */
+    float *q_scales;
+    size_t quant_group;
+} qvl_row_tail;
+
+/* qvl_linear_q16_i8_multi (or, with swiglu_pair = 1 and two matrices, the
+ * gate/up + SwiGLU product of qvl_gate_up_swiglu_q16_i8 writing C[0]) plus
+ * the fused row tail.  One launch when M <= 4 and group_size >= 128; other
+ * shapes run the same steps as separate launches. */
+int qvl_linear_q16_i8_tail(const int16_t *q, const float *q_scales, size_t n_mats,
+                           const int8_t *const *B, const float *const *B_scales, float *const *C,
+                           const size_t *N, size_t M, size_t K, size_t group_size, int semantics,
+                           int swiglu_pair, const qvl_row_tail *tail, void *stream);
+
+/* Batched products on the tensor cores (tcgen05 kind::i8), the reference's
+ * M>1 (TILED) order: the int16 activations q [M, K] (qvl_quantize_rows /
+ * qvl_rms_norm_i8 output, per-row quantisation: one scale per row) are split
+ * once into the workspace (qvl_linear_q16_i8_batched_workspace_bytes) and
+ * reused by every matrix; per-row weight scales (group = K), K % 128 == 0,
+ * N[i] >= 128, M >= 16.  QVL_SEM_ACCUMULATE adds into C.  swiglu_pair = 1:
+ * two matrices (gate, up) and C[0] = swiglu(gate, up) with up in up_scratch. */
+size_t qvl_linear_q16_i8_batched_workspace_bytes(size_t M, size_t K);
+int qvl_linear_q16_i8_batched(const int16_t *q, const float *q_scales, size_t n_mats,
+                              const int8_t *const *B, const float *const *B_scales, float *const *C,
+                              const size_t *N, size_t M, size_t K, int semantics, int swiglu_pair,
+                              float *up_scratch, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- SwiGLU (layers/src/text_layer.cpp:420-434) ------------------------
  * gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i], in place, n elements. */
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import (argmax, attention, embedding_i8, linear_i8, ref_attention, ref_embedding_i8,
+from . import (TILED, argmax, attention, embedding_i8, linear_i8, ref_attention, ref_embedding_i8,
                ref_i8_kernel, ref_rms_norm_i8, ref_rope, ref_swiglu, rms_norm_i8, rope_inplace,
                swiglu)
 
@@ -21,10 +21,15 @@ def _f16(a):
 
 
 class CpuDecoder:
-    def __init__(self, cfg, w: dict, max_ctx: int, cos: np.ndarray, sin: np.ndarray, backend="ref"):
+    def __init__(self, cfg, w: dict, max_ctx: int, cos: np.ndarray, sin: np.ndarray, backend="ref",
+                 order="lane8"):
+        """order: "lane8" = the reference's M=1 decode GEMV order (what it
+        runs per token); "tiled" = its M>1 kernel order (restatement only),
+        for checking a batch computed as one M=B product."""
         self.cfg, self.w, self.S = cfg, w, max_ctx
         self.cos, self.sin = cos, sin
-        self.backend = backend
+        self.backend = backend if order == "lane8" else "orc"
+        self.order = order
         L, NKV, D = cfg.layers, cfg.kv_heads, cfg.head_dim
         self.kc = np.zeros((L, NKV, max_ctx, D), np.float32)
         self.vc = np.zeros((L, NKV, max_ctx, D), np.float32)
@@ -33,6 +38,8 @@ class CpuDecoder:
     def _lin(self, x, W, S):
         x = x.reshape(1, -1)
         K = x.shape[1]
+        if self.order == "tiled":
+            return linear_i8(x, W, S, K, TILED)[0]
         if self.backend == "ref":
             return ref_i8_kernel(x, W, S, K)[0]
         return linear_i8(x, W, S, K)[0]

@@ -44,6 +44,7 @@ EXPORTED = (
     "qvl_attention_workspace_bytes", "qvl_attention_decode", "qvl_argmax_rows",
     "qvl_qknorm_rope_kv_append", "qvl_rms_norm_i8", "qvl_embedding_lookup_i8",
     "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
+    "qvl_linear_q16_i8_tail", "qvl_linear_q16_i8_batched", "qvl_linear_q16_i8_batched_workspace_bytes",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -56,6 +57,13 @@ class AttnDims(ctypes.Structure):
     _fields_ = [("num_heads", ctypes.c_int), ("num_kv_heads", ctypes.c_int),
                 ("head_dim", ctypes.c_int), ("page_size", ctypes.c_int),
                 ("max_pages_per_seq", ctypes.c_int), ("max_pos", ctypes.c_int)]
+
+
+class RowTail(ctypes.Structure):
+    _fields_ = [("counter", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_s", ctypes.c_void_p),
+                ("norm_group", ctypes.c_size_t), ("eps", ctypes.c_float), ("inplace_form", ctypes.c_int),
+                ("norm_out", ctypes.c_void_p), ("q", ctypes.c_void_p), ("q_scales", ctypes.c_void_p),
+                ("quant_group", ctypes.c_size_t)]
 
 
 _P, _Z, _I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
@@ -93,6 +101,11 @@ def load_library(path: str = LIB_PATH):
     L.qvl_embedding_lookup_i8.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
     L.qvl_swiglu_quantize_rows.argtypes = [_P] * 4 + [_Z, _Z, _Z, _P]
     L.qvl_gate_up_swiglu_q16_i8.argtypes = [_P] * 8 + [_Z, _Z, _Z, _Z, _I, _P]
+    L.qvl_linear_q16_i8_tail.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _Z, _I, _I,
+                                         ctypes.POINTER(RowTail), _P]
+    L.qvl_linear_q16_i8_batched_workspace_bytes.restype = _Z
+    L.qvl_linear_q16_i8_batched_workspace_bytes.argtypes = [_Z, _Z]
+    L.qvl_linear_q16_i8_batched.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _I, _I, _P, _P, _Z, _P]
     L.qvl_linear_q16_i8_multi.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _Z, _I, _P]
     _lib = L
     return L
@@ -324,3 +337,42 @@ def gate_up_swiglu(q, q_scales, w_gate, s_gate, w_up, s_up, h, group_size, up_sc
                                                     K, group_size, semantics, _stream(stream)),
            "gate_up_swiglu")
     return h
+
+
+def linear_tail(q, q_scales, mats, outs, group_size, counter, q_out, q_out_scales, quant_group,
+                norm=None, eps=1e-6, inplace_form=False, norm_out=None, swiglu_pair=False,
+                semantics=SEM_REFERENCE, stream=None):
+    """Products of `mats` (like linear_q16_multi; swiglu_pair=True: gate/up with
+    SwiGLU into outs[0]) followed, in the same launch, by RMSNorm (norm=(w, s,
+    group)) and/or quantisation of outs[0] into q_out/q_out_scales.
+    `counter`: a zero-initialised int32 device tensor (left at zero)."""
+    n = len(mats)
+    M, K = q.shape
+    Bp = (ctypes.c_void_p * n)(*[_ptr(w) for w, _ in mats])
+    Sp = (ctypes.c_void_p * n)(*[_ptr(s) for _, s in mats])
+    Cp = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    Np = (ctypes.c_size_t * n)(*[w.shape[0] for w, _ in mats])
+    t = RowTail(_ptr(counter), _ptr(norm[0]) if norm else None, _ptr(norm[1]) if norm else None,
+                norm[2] if norm else 0, eps, int(inplace_form), _ptr(norm_out), _ptr(q_out),
+                _ptr(q_out_scales), quant_group)
+    _check(load_library().qvl_linear_q16_i8_tail(_ptr(q), _ptr(q_scales), n, Bp, Sp, Cp, Np, M, K, group_size,
+                                                 semantics, int(swiglu_pair), ctypes.byref(t), _stream(stream)),
+           "linear_tail")
+    return outs
+
+
+def linear_batched(q, q_scales, mats, outs, workspace, semantics=SEM_TILED, swiglu_pair=False, up_scratch=None,
+                   stream=None):
+    """Tensor-core products of the same activations (split into hi/lo planes once)."""
+    n = len(mats)
+    M, K = q.shape
+    Bp = (ctypes.c_void_p * n)(*[_ptr(w) for w, _ in mats])
+    Sp = (ctypes.c_void_p * n)(*[_ptr(s) for _, s in mats])
+    Cp = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    Np = (ctypes.c_size_t * n)(*[w.shape[0] for w, _ in mats])
+    L = load_library()
+    ws = workspace.get(L.qvl_linear_q16_i8_batched_workspace_bytes(M, K))
+    _check(L.qvl_linear_q16_i8_batched(_ptr(q), _ptr(q_scales), n, Bp, Sp, Cp, Np, M, K, semantics,
+                                       int(swiglu_pair), _ptr(up_scratch), _ptr(ws), ws.numel(), _stream(stream)),
+           "linear_batched")
+    return outs

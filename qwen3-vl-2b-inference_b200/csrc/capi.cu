@@ -227,6 +227,103 @@ int qvl_gate_up_swiglu_q16_i8(const int16_t *q, const float *q_scales, const int
     return QVL_OK;
 }
 
+int qvl_linear_q16_i8_tail(const int16_t *q, const float *q_scales, size_t n_mats,
+                           const int8_t *const *B, const float *const *B_scales, float *const *C,
+                           const size_t *N, size_t M, size_t K, size_t group_size, int semantics,
+                           int swiglu_pair, const qvl_row_tail *tail, void *stream) {
+    if (!q || !q_scales || !B || !B_scales || !C || !N || !tail || !tail->counter || !tail->q ||
+        !tail->q_scales || n_mats == 0 || n_mats > 3)
+        return QVL_ERR_INVALID;
+    if (swiglu_pair && (n_mats != 2 || N[0] != N[1])) return QVL_ERR_INVALID;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    const int sem = semantics & ~QVL_SEM_ACCUMULATE;
+    if (sem < QVL_SEM_REFERENCE || sem > QVL_SEM_TILED) return QVL_ERR_INVALID;
+    const size_t H = N[0];
+    if (H % 16 || H > 16384 || tail->quant_group == 0 || tail->quant_group % 16 || H % tail->quant_group ||
+        H / tail->quant_group > 64 || (tail->norm_w && (!tail->norm_s || tail->norm_group == 0 ||
+                                                         H % tail->norm_group)))
+        return QVL_ERR_UNSUPPORTED;
+    size_t total = 0;
+    for (size_t i = 0; i < n_mats; ++i) {
+        if (!B[i] || !B_scales[i] || !C[i] || !aligned(B[i], 16)) return QVL_ERR_INVALID;
+        int rc = check_linear_shape(M, N[i], K, group_size);
+        if (rc) return rc;
+        total += N[i];
+    }
+    if (!aligned(q, 16) || !aligned(C[0], 16) || total > (size_t)INT32_MAX) return QVL_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool lane8 = lane8_for(sem, M, N[0], K);
+    if (qvl::gemv_fast_eligible((int)M, (int)K, (int)group_size)) {
+        qvl::GemvArgs a = {};
+        a.q = q; a.qs = q_scales; a.M = (int)M; a.K = (int)K; a.g = (int)group_size; a.acc = acc;
+        size_t end = 0;
+        for (size_t i = 0; i < 3; ++i) {
+            if (i < n_mats) {
+                a.segs.W[i] = B[i]; a.segs.ws[i] = B_scales[i]; a.segs.y[i] = C[i];
+                a.segs.ldy[i] = (long)N[i];
+                end += N[i];
+            }
+            a.segs.end[i] = (int)end;
+        }
+        a.segs.nseg = (int)n_mats;
+        a.N = (int)total;
+        a.pair = swiglu_pair ? 1 : 0;
+        a.tail.counter = tail->counter;
+        a.tail.x = C[0];
+        a.tail.wq = tail->norm_w; a.tail.ws = tail->norm_s; a.tail.ngs = (int)tail->norm_group;
+        a.tail.eps = tail->eps; a.tail.inplace_form = tail->inplace_form;
+        a.tail.out = tail->norm_out; a.tail.q = tail->q; a.tail.qs = tail->q_scales;
+        a.tail.qg = (int)tail->quant_group; a.tail.H = (int)H; a.tail.rows = (int)M;
+        QVL_CUDA_TRY(qvl::launch_gemv_i8(a, lane8, st));
+        return QVL_OK;
+    }
+    // separate launches
+    if (swiglu_pair) {
+        return QVL_ERR_UNSUPPORTED;   // needs an up buffer: use qvl_gate_up_swiglu_q16_i8 + qvl_quantize_rows
+    }
+    for (size_t i = 0; i < n_mats; ++i) {
+        int rc = run_q16_linear(q, q_scales, B[i], B_scales[i], C[i], M, N[i], K, group_size,
+                                lane8_for(sem, M, N[i], K), st, acc);
+        if (rc) return rc;
+    }
+    QVL_CUDA_TRY(qvl::launch_rmsnorm_quant(C[0], tail->norm_w, tail->norm_s, tail->norm_out, tail->q,
+                                           tail->q_scales, (int)M, (int)H, (int)(tail->norm_w ? tail->norm_group : H),
+                                           tail->eps, tail->inplace_form != 0, (int)tail->quant_group, st));
+    return QVL_OK;
+}
+
+size_t qvl_linear_q16_i8_batched_workspace_bytes(size_t M, size_t K) {
+    return qvl::gemm_tc_planes_bytes(M, K);
+}
+
+int qvl_linear_q16_i8_batched(const int16_t *q, const float *q_scales, size_t n_mats,
+                              const int8_t *const *B, const float *const *B_scales, float *const *C,
+                              const size_t *N, size_t M, size_t K, int semantics, int swiglu_pair,
+                              float *up_scratch, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!q || !q_scales || !B || !B_scales || !C || !N || n_mats == 0 || n_mats > 3) return QVL_ERR_INVALID;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    const int sem = semantics & ~QVL_SEM_ACCUMULATE;
+    if (sem != QVL_SEM_TILED && !(sem == QVL_SEM_REFERENCE && M > 1)) return QVL_ERR_UNSUPPORTED;
+    if (swiglu_pair && (n_mats != 2 || N[0] != N[1] || !up_scratch || acc)) return QVL_ERR_INVALID;
+    for (size_t i = 0; i < n_mats; ++i) {
+        if (!B[i] || !B_scales[i] || !C[i] || !aligned(B[i], 16)) return QVL_ERR_INVALID;
+        if (!qvl::gemm_tc_supported(M, N[i], K, K)) return QVL_ERR_UNSUPPORTED;
+    }
+    const size_t need = qvl::gemm_tc_planes_bytes(M, K);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    int8_t *hi = static_cast<int8_t *>(workspace);
+    uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + need / 2;
+    QVL_CUDA_TRY(qvl::launch_split_hi_lo(q, hi, lo, (int)M, (int)K, st));
+    for (size_t i = 0; i < n_mats; ++i) {
+        float *out = (swiglu_pair && i == 1) ? up_scratch : C[i];
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo, q_scales, B[i], B_scales[i], out, (int)M, (int)N[i],
+                                                   (int)K, acc, st));
+    }
+    if (swiglu_pair) QVL_CUDA_TRY(qvl::launch_swiglu(C[0], up_scratch, (long)(M * N[0]), st));
+    return QVL_OK;
+}
+
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
     if (!gate || !up) return QVL_ERR_INVALID;
     if (n == 0) return QVL_OK;

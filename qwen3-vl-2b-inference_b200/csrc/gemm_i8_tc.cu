@@ -48,7 +48,7 @@ template <int NT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
                   const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
-                  const float *__restrict w_scale, float *__restrict C, int M, int N, int K) {
+                  const float *__restrict w_scale, float *__restrict C, int M, int N, int K, int acc) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -146,7 +146,9 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
                 if (m < M && n < N) {
                     const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
                     const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
-                    C[(size_t)m * N + n] = fma_rn(p, ws, 0.0f);
+                    const float v = fma_rn(p, ws, 0.0f);
+                    float *cp = C + (size_t)m * N + n;
+                    *cp = acc ? add_rn(*cp, v) : v;   // residual add (add_vector order)
                 }
             }
         }
@@ -212,7 +214,7 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
 
 template <int NT>
 cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
-                      const float *ws, float *C, int M, int N, int K, cudaStream_t st) {
+                      const float *ws, float *C, int M, int N, int K, int acc, cudaStream_t st) {
     auto kern = gemm_i8_tc_kernel<NT>;
     const int smem = TcSmem<NT>::kBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -227,7 +229,7 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K);
+    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
 }
 
 }  // namespace
@@ -238,30 +240,38 @@ bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
 
 size_t gemm_tc_planes_bytes(size_t M, size_t K) { return 2 * ((M * K + 255) & ~(size_t)255); }
 
-cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,
-                              const float *ws, float *C, int M, int N, int K, cudaStream_t stream) {
-    {
-        cudaLaunchConfig_t cfg = {};
-        const long n = (long)M * K;
-        long blocks = (n / 8 + 255) / 256;
-        cfg.gridDim = dim3((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8));
-        cfg.blockDim = dim3(256);
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, split_hi_lo_kernel, q, hi, lo, n);
-        if (e != cudaSuccess) return e;
-    }
+cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M, int K, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    const long n = (long)M * K;
+    long blocks = (n / 8 + 255) / 256;
+    cfg.gridDim = dim3((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, split_hi_lo_kernel, q, hi, lo, n);
+}
+
+cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
+                                     const float *ws, float *C, int M, int N, int K, int acc,
+                                     cudaStream_t stream) {
     const int NT = M >= 256 ? 128 : (M >= 64 ? 64 : 32);
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
-    if (NT == 128) return launch_nt<128>(mw, mh, ml, qs, ws, C, M, N, K, stream);
-    if (NT == 64) return launch_nt<64>(mw, mh, ml, qs, ws, C, M, N, K, stream);
-    return launch_nt<32>(mw, mh, ml, qs, ws, C, M, N, K, stream);
+    if (NT == 128) return launch_nt<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 64) return launch_nt<64>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    return launch_nt<32>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+}
+
+cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,
+                              const float *ws, float *C, int M, int N, int K, cudaStream_t stream) {
+    cudaError_t e = launch_split_hi_lo(q, hi, lo, M, K, stream);
+    if (e != cudaSuccess) return e;
+    return launch_gemm_i8_tc_planes(hi, lo, qs, W, ws, C, M, N, K, 0, stream);
 }
 
 }  // namespace qvl

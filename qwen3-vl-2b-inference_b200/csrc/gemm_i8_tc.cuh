@@ -11,4 +11,10 @@ bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g);
 size_t gemm_tc_planes_bytes(size_t M, size_t K);
 cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,
                               const float *ws, float *C, int M, int N, int K, cudaStream_t stream);
+// hi/lo planes from int16 activations, and the GEMM on planes already split
+// (so several products of the same activations split once).  acc: C += result.
+cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M, int K, cudaStream_t stream);
+cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
+                                     const float *ws, float *C, int M, int N, int K, int acc,
+                                     cudaStream_t stream);
 }  // namespace qvl

@@ -23,6 +23,7 @@
 // follows the reference operation by operation, so outputs are bit-exact.
 #include "common.cuh"
 #include "gemv_common.cuh"
+#include "tail.cuh"
 
 namespace qvl {
 
@@ -39,7 +40,7 @@ constexpr int fast_min_blocks() { return (MR == 1 && IT <= 4) ? 6 : 1; }
 template <int MR, bool LANE, int IT>
 __global__ void __launch_bounds__(kThreads, fast_min_blocks<MR, IT>())
 gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs, GemvSegs sg,
-                    int M, int N, int K, int g, int acc, int seglog, int pair) {
+                    int M, int N, int K, int g, int acc, int seglog, int pair, RowTail tail) {
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *q_s = reinterpret_cast<int16_t *>(smem);
     const int G = K / g;
@@ -214,6 +215,7 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs, Gem
             if (nn < N) issue(nn, wr, wsr);
         }
     }
+    if (tail.counter) run_row_tail(tail, smem);   // last CTA: RMSNorm / quantisation of the finished rows
 }
 
 namespace {
@@ -221,6 +223,7 @@ template <int MR, bool LANE, int IT>
 cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
     const int G = a.K / a.g;
     size_t smem = (size_t)MR * a.K * sizeof(int16_t) + (size_t)MR * G * sizeof(float);
+    if (a.tail.counter && row_tail_smem(a.tail.H, a.tail.wq) > smem) smem = row_tail_smem(a.tail.H, a.tail.wq);
     auto kern = gemv_i8_fast_kernel<MR, LANE, IT>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -250,7 +253,8 @@ cudaError_t launch_fast_t(const GemvArgs &a, cudaStream_t stream) {
     cfg.numAttrs = 1;
     GemvSegs sg = a.segs;
     if (sg.nseg == 0) sg = GemvSegs::single(a.W, a.ws, a.y, a.N, a.ldy);
-    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, sg, a.M, sg.total(), a.K, a.g, a.acc, seglog, a.pair);
+    return cudaLaunchKernelEx(&cfg, kern, a.q, a.qs, sg, a.M, sg.total(), a.K, a.g, a.acc, seglog, a.pair,
+                              a.tail);
 }
 
 template <int MR, bool LANE>

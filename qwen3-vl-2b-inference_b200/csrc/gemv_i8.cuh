@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstddef>
+#include "tail.cuh"
 
 namespace qvl {
 
@@ -40,6 +41,7 @@ struct GemvArgs {
     int acc;            // 1: y += result (fused residual add), 0: y = result
     GemvSegs segs;      // nseg > 0: several matrices (fast path only); W/ws/y/N unused
     int pair;           // segs = {gate, up} of equal rows: y0 = swiglu(gate, up) (fast path only)
+    RowTail tail;       // tail.counter != nullptr: fused RMSNorm / quantisation (fast path only)
 };
 
 bool gemv_shape_supported(int K, int g);

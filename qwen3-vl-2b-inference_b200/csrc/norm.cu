@@ -10,83 +10,27 @@
 // inv_rms = (float)(1.0 / (double)sqrtf(a)) for rms_norm and 1.0f / sqrtf(a)
 // for rms_norm_inplace; out[j] = (float)wq[j] * ((ws[j/gs] * inv_rms) * x[j]).
 #include "common.cuh"
-#include "qact.cuh"
+#include "tail.cuh"
 #include "norm.cuh"
 
 namespace qvl {
-
-// Sum of squares in the reference's lane order, by warp 0 of the CTA; the
-// result is valid in every lane of warp 0.
-__device__ __forceinline__ float rms_sumsq_ref(const float *xs, int H) {
-    const int lane = threadIdx.x & 31;
-    const int l = lane & 7;
-    float acc = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < H; i += 8) {
-        const float v = xs[i + l];
-        acc = add_rn(acc, mul_rn(v, v));
-    }
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) ss = add_rn(ss, __shfl_sync(0xffffffffu, acc, k));
-    return ss;
-}
-
-__device__ __forceinline__ float rms_inv(float ss, int H, float eps, bool inplace_form) {
-    const float inv_hs = __fdiv_rn(1.0f, (float)H);
-    const float a = fma_rn(ss, inv_hs, eps);
-    const float r = __fsqrt_rn(a);
-    return inplace_form ? __fdiv_rn(1.0f, r) : __double2float_rn(1.0 / (double)r);
-}
 
 // grid: rows; block 256; dynamic smem 2*H floats.
 // out (nullable) receives the normalised row; q/qs (nullable) its
 // quantisation with group qg (bit-exact with quantize_rows on `out`).
 __global__ void __launch_bounds__(256)
-rmsnorm_quant_kernel(const float *__restrict x, const int8_t *__restrict wq,
-                     const float *__restrict ws, float *__restrict out, int16_t *__restrict q,
+rmsnorm_quant_kernel(const float *x, const int8_t *__restrict wq,
+                     const float *__restrict ws, float *out, int16_t *__restrict q,
                      float *__restrict qs, int H, int ngs, float eps, int inplace_form, int qg) {
     extern __shared__ __align__(16) float sm[];
-    float *xs = sm;
-    float *ts = sm + H;
-    __shared__ float inv_sh;
-    __shared__ float qinv[64];
+    __shared__ float scratch[65];
     pdl_launch_dependents();
     pdl_wait();
     const int row = blockIdx.x;
-    const float *xr = x + (size_t)row * H;
-    for (int i = threadIdx.x; i < H / 4; i += blockDim.x)
-        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(xr)[i];
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        const float ss = rms_sumsq_ref(xs, H);
-        if (threadIdx.x == 0) inv_sh = rms_inv(ss, H, eps, inplace_form != 0);
-    }
-    __syncthreads();
-    const float inv = inv_sh;
-    for (int j = threadIdx.x; j < H; j += blockDim.x) {
-        const float t = mul_rn((float)wq[j], mul_rn(mul_rn(ws[j / ngs], inv), xs[j]));
-        ts[j] = t;
-        if (out) out[(size_t)row * H + j] = t;
-    }
-    if (!q) return;
-    __syncthreads();
-    const int G = H / qg;
-    const int hw = threadIdx.x >> 4, nhw = blockDim.x >> 4, t16 = threadIdx.x & 15;
-    // both half-warps of a warp take the same trip count (full-mask shuffles)
-    for (int e0 = hw & ~1; e0 < G; e0 += nhw) {
-        const int e_raw = e0 + (hw & 1);
-        const bool active = e_raw < G;
-        const int e = active ? e_raw : e0;
-        const float s = group_scale_ref(ts + (size_t)e * qg, qg, t16);
-        if (active && t16 == 0) {
-            qs[(size_t)row * G + e] = s;
-            qinv[e] = __fdiv_rn(1.0f, s);
-        }
-    }
-    __syncthreads();
-    for (int j = threadIdx.x; j < H; j += blockDim.x)
-        q[(size_t)row * H + j] = quant_one(ts[j], qinv[j / qg]);
+    const int G = q ? H / qg : 0;
+    cta_norm_quant_row(x + (size_t)row * H, wq, ws, ngs, eps, inplace_form != 0,
+                       out ? out + (size_t)row * H : nullptr, q ? q + (size_t)row * H : nullptr,
+                       q ? qs + (size_t)row * G : nullptr, qg, H, sm, sm + H, scratch);
 }
 
 // grid: n_tokens; block 256.  out[t] = (float)table[id] * scale[id]

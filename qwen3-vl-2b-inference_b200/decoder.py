@@ -28,9 +28,9 @@ import dataclasses
 import numpy as np
 import torch
 
-from . import (SEM_ACCUMULATE, SEM_LANE8, PagedKV, Workspace, attention, embedding_lookup_i8,
-               gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, qknorm_rope_kv_append,
-               rms_norm_i8)
+from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Workspace, attention, embedding_lookup_i8,
+               gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
+               qknorm_rope_kv_append, rms_norm_i8)
 from . import load_library
 
 
@@ -107,7 +107,12 @@ class TextDecoder:
     """Batched decode over a paged FP16 KV cache (one sequence per request)."""
 
     def __init__(self, weights: TextWeights, max_batch: int, max_ctx: int, page_size: int = 64,
-                 device="cuda"):
+                 device="cuda", batch_order: str = "auto"):
+        """batch_order: "lane8" computes every request row in the reference's
+        M=1 decode order (CUDA-core GEMV, each request bit-matches the
+        reference run on it alone); "tiled" runs the batch as one M=B product
+        on the tensor cores in the reference's M>1 order (what the reference's
+        linear() does for an M>1 call); "auto" = tiled for B >= 16."""
         self.w = weights
         cfg = self.cfg = weights.cfg
         self.B = max_batch
@@ -137,6 +142,14 @@ class TextDecoder:
                    for _ in range(cfg.layers)]
         cos, sin = rope_table(max_ctx, D, cfg.rope_theta)
         self.set_rope_table(cos, sin)
+        self.counters = torch.zeros(4, dtype=torch.int32, device=dev)   # fused-tail counters (stay 0)
+        self.fuse_tails = max_batch == 1   # one CTA finishes each row: pays off for a single row
+        if batch_order == "auto":
+            batch_order = "tiled" if max_batch >= 16 else "lane8"
+        self.use_tc = batch_order == "tiled"
+        self.tc_ws = Workspace(dev)
+        if self.use_tc:
+            self.tc_ws.get(load_library().qvl_linear_q16_i8_batched_workspace_bytes(max_batch, cfg.intermediate))
         self.ws = Workspace(dev)
         self.ws.get(load_library().qvl_attention_workspace_bytes(B, max_ctx, self.kv[0].dims))
 
@@ -167,25 +180,83 @@ class TextDecoder:
         qx, qx_s = self.qx[:B], self.qx_s[:B]
         seq, pos = self.seq_ids[:B], self.positions[:B]
         embedding_lookup_i8(t["embed"], t["embed_s"], self.tokens[:B], x)
-        for l in range(cfg.layers):
-            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+        if self.use_tc:
+            self._step_tc(B)
+            greedy_decode(self.logits[:B], out=self.tokens[:B])
+            pos.add_(1)
+            return
+        if self.fuse_tails:
+            rms_norm_i8(x, t["in_norm"][0], t["in_norm_s"][0], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+        L = cfg.layers
+        for l in range(L):
+            if not self.fuse_tails:
+                rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
             self._lin_multi(qx, qx_s, ("wq", "wk", "wv"), l, (self.q[:B], self.k[:B], self.v[:B]))
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
             attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
             _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
+            if self.fuse_tails:
+                # o_proj + residual, then post-attention rms_norm -> gate/up input, one launch
+                linear_tail(self.qa[:B], self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], H, self.counters[0],
+                            qx, qx_s, H, norm=(t["post_norm"][l], t["post_norm_s"][l], ng), eps=eps,
+                            semantics=SEM_LANE8 | SEM_ACCUMULATE)
+                # gate/up + SwiGLU, then quantisation of the SwiGLU row -> down input
+                linear_tail(qx, qx_s, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
+                            [self.gate[:B], self.up[:B]], H, self.counters[1], self.qh[:B], self.qh_s[:B],
+                            cfg.intermediate, swiglu_pair=True, semantics=SEM_LANE8)
+                # down + residual, then the next layer's input rms_norm (or the final norm) -> next input
+                if l + 1 < L:
+                    nrm, inpl, nout = (t["in_norm"][l + 1], t["in_norm_s"][l + 1], ng), False, None
+                else:
+                    nrm, inpl, nout = (t["final_norm"], t["final_norm_s"], ng), True, x
+                linear_tail(self.qh[:B], self.qh_s[:B], [(t["wd"][l], t["wd_s"][l])], [x], cfg.intermediate,
+                            self.counters[2], qx, qx_s, H, norm=nrm, eps=eps, inplace_form=inpl, norm_out=nout,
+                            semantics=SEM_LANE8 | SEM_ACCUMULATE)
+                continue
             self._lin(self.qa[:B], self.qa_s[:B], "wo", l, x, acc=True)
             rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
             gate_up_swiglu(qx, qx_s, t["wg"][l], t["wg_s"][l], t["wu"][l], t["wu_s"][l], self.gate[:B], H,
                            up_scratch=self.up[:B], semantics=SEM_LANE8)
             _quantize_into(self.gate[:B], self.qh[:B], self.qh_s[:B])
             self._lin(self.qh[:B], self.qh_s[:B], "wd", l, x, acc=True)
-        rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s, quant_group=H,
-                    inplace_form=True)
+        if not self.fuse_tails:
+            rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s,
+                        quant_group=H, inplace_form=True)
         self._lin(qx, qx_s, "embed", None, self.logits[:B])
         greedy_decode(self.logits[:B], out=self.tokens[:B])
         pos.add_(1)
+
+    def _step_tc(self, B):
+        """Tensor-core batch (reference M>1 order): every linear runs as one
+        M=B tcgen05 product; activations are split into hi/lo planes once per
+        distinct input."""
+        cfg, t = self.cfg, self.w.t
+        H, ng, eps = cfg.hidden, cfg.norm_group, cfg.eps
+        x, qx, qx_s = self.x[:B], self.qx[:B], self.qx_s[:B]
+        seq, pos = self.seq_ids[:B], self.positions[:B]
+        ws = self.tc_ws
+        for l in range(cfg.layers):
+            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+            linear_batched(qx, qx_s, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
+                           [self.q[:B], self.k[:B], self.v[:B]], ws)
+            qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
+                                  self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
+                                  t["k_norm_s"][l], ng, eps)
+            attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+            _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
+            linear_batched(self.qa[:B], self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], ws,
+                           semantics=SEM_TILED | SEM_ACCUMULATE)
+            rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
+            linear_batched(qx, qx_s, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
+                           [self.gate[:B], self.up[:B]], ws, swiglu_pair=True, up_scratch=self.up[:B])
+            _quantize_into(self.gate[:B], self.qh[:B], self.qh_s[:B])
+            linear_batched(self.qh[:B], self.qh_s[:B], [(t["wd"][l], t["wd_s"][l])], [x], ws,
+                           semantics=SEM_TILED | SEM_ACCUMULATE)
+        rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s, quant_group=H,
+                    inplace_form=True)
+        linear_batched(qx, qx_s, [(t["embed"], t["embed_s"])], [self.logits[:B]], ws)
 
     # launches of our kernels per step (attention = 3 kernels)
     def kernels_per_step(self):
