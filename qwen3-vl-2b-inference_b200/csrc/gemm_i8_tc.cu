@@ -20,6 +20,7 @@
 // read the accumulators (tcgen05.ld) for the epilogue.  Every wait is bounded.
 #include <cstdio>
 #include <mutex>
+#include <cooperative_groups.h>
 #include "tc_common.cuh"
 #include "gemm_i8_tc.cuh"
 
@@ -43,8 +44,11 @@ struct TcSmem {
     static constexpr int kBytes = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
 };
 
-// grid: (ceil(N/128), ceil(M/NT)); block 128.
-template <int NT>
+// grid: (ceil(N/128), ceil(M/NT), SPLIT); block 128; with SPLIT > 1 the SPLIT
+// CTAs of a cluster (1, 1, SPLIT) each take K/SPLIT and their exact int32
+// partial sums are added through distributed shared memory (split-K keeps
+// small-N products -- decode batches -- spread over the GPU).
+template <int NT, int SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
                   const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
@@ -62,7 +66,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kBM;
     const int m0 = blockIdx.y * NT;
-    const int nk = K / kBK;
+    const int nk = K / kBK / SPLIT;             // stages of this CTA's K slice
+    const int kb0 = blockIdx.z * nk;
     constexpr uint32_t kCols = (2 * NT < 32) ? 32 : 2 * NT;   // power of two >= 32
 
     if (threadIdx.x == 0) {
@@ -96,10 +101,10 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
             if (!ok) break;
             unsigned char *st = smem + s * L::kStage;
             tc::mbar_expect_tx(full0 + 8 * s, L::kStage);
-            tc::tma_load_2d(tc::smem_u32(st), &tm_w, kb * kBK, n0, full0 + 8 * s);
+            tc::tma_load_2d(tc::smem_u32(st), &tm_w, (kb0 + kb) * kBK, n0, full0 + 8 * s);
             if (kb == 0) pdl_wait();   // activations come from the previous kernel
-            tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, kb * kBK, m0, full0 + 8 * s);
-            tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, kb * kBK, m0, full0 + 8 * s);
+            tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, (kb0 + kb) * kBK, m0, full0 + 8 * s);
+            tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, (kb0 + kb) * kBK, m0, full0 + 8 * s);
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
@@ -130,10 +135,39 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     pdl_wait();   // activation scales and C belong to the stream order
     const bool acc_ok = tc::mbar_wait(accbar, 0, &g_gemm_tc_timeout);
     tc::tc_fence_after();
-    if (acc_ok) {
-        const int n = n0 + warp * 32 + lane;
-        const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
+    if constexpr (SPLIT == 1) {
+        if (acc_ok) {
+            const int n = n0 + warp * 32 + lane;
+            const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
+            const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+#pragma unroll 1
+            for (int c0 = 0; c0 < NT; c0 += 16) {
+                uint32_t hi[16], lo[16];
+                tc::tmem_ld16(d_hi + lane_off + c0, hi);
+                tc::tmem_ld16(d_lo + lane_off + c0, lo);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m < M && n < N) {
+                        const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
+                        const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
+                        const float v = fma_rn(p, ws, 0.0f);
+                        float *cp = C + (size_t)m * N + n;
+                        *cp = acc ? add_rn(*cp, v) : v;   // residual add (add_vector order)
+                    }
+                }
+            }
+        }
+    } else {
+        // partial integer sums of this K slice -> shared memory [128 rows][NT]
+        // (the stage ring is idle now), then rank r of the cluster adds the
+        // SPLIT partials of rows [r*128/SPLIT, (r+1)*128/SPLIT) and finishes them.
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        int32_t *part = reinterpret_cast<int32_t *>(smem);
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const int row = warp * 32 + lane;
 #pragma unroll 1
         for (int c0 = 0; c0 < NT; c0 += 16) {
             uint32_t hi[16], lo[16];
@@ -141,17 +175,25 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
             tc::tmem_ld16(d_lo + lane_off + c0, lo);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int m = m0 + c0 + j;
-                if (m < M && n < N) {
-                    const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
-                    const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
-                    const float v = fma_rn(p, ws, 0.0f);
-                    float *cp = C + (size_t)m * N + n;
-                    *cp = acc ? add_rn(*cp, v) : v;   // residual add (add_vector order)
-                }
+            for (int j = 0; j < 16; ++j) part[row * NT + c0 + j] = acc_ok ? (int)(hi[j] * 256u + lo[j]) : 0;
+        }
+        cluster.sync();
+        const int rank = (int)cluster.block_rank();
+        constexpr int kRows = kBM / SPLIT;
+        for (int e = threadIdx.x; e < kRows * NT; e += kThreads) {
+            const int r = rank * kRows + e / NT, j = e % NT;
+            uint32_t S = 0;
+#pragma unroll
+            for (int k = 0; k < SPLIT; ++k) S += (uint32_t)cluster.map_shared_rank(part, k)[r * NT + j];
+            const int n = n0 + r, m = m0 + j;
+            if (acc_ok && m < M && n < N) {
+                const float p = mul_rn(__int2float_rn((int)S), __ldg(a_scale + m));
+                const float v = fma_rn(p, __ldg(w_scale + n), 0.0f);
+                float *cp = C + (size_t)m * N + n;
+                *cp = acc ? add_rn(*cp, v) : v;
             }
         }
+        cluster.sync();   // partials stay alive until every rank has read them
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -212,23 +254,27 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT>
+template <int NT, int SPLIT>
 cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
                       const float *ws, float *C, int M, int N, int K, int acc, cudaStream_t st) {
-    auto kern = gemm_i8_tc_kernel<NT>;
+    auto kern = gemm_i8_tc_kernel<NT, SPLIT>;
     const int smem = TcSmem<NT>::kBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + kBM - 1) / kBM, (M + NT - 1) / NT);
+    cfg.gridDim = dim3((N + kBM - 1) / kBM, (M + NT - 1) / NT, SPLIT);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = SPLIT;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = SPLIT > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
 }
 
@@ -262,9 +308,17 @@ cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const 
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
-    if (NT == 128) return launch_nt<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    if (NT == 64) return launch_nt<64>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    return launch_nt<32>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 128) return launch_nt<128, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 64) return launch_nt<64, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    // small M (decode batches): split K over a cluster until ~2 CTAs per SM
+    const long tiles = (long)((N + kBM - 1) / kBM) * ((M + 31) / 32);
+    const int nkb = K / kBK;
+    int split = 1;
+    while (split < 8 && tiles * split * 2 <= 2 * 148 && nkb % (split * 2) == 0) split *= 2;
+    if (split == 8) return launch_nt<32, 8>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (split == 4) return launch_nt<32, 4>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (split == 2) return launch_nt<32, 2>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    return launch_nt<32, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
 }
 
 cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,

@@ -232,7 +232,8 @@ def test_argmax_tie_and_nan(qvl, cuda):
 
 
 # ------------------------------------------------------------ tensor-core GEMM
-@pytest.mark.parametrize("M,N,K", [(16, 128, 128), (512, 2048, 2048), (512, 1024, 2048), (512, 6144, 2048),
+@pytest.mark.parametrize("M,N,K", [(16, 128, 128), (32, 2048, 2048), (32, 1024, 2048), (32, 2048, 6144),
+                                   (17, 256, 1024), (48, 6144, 2048), (512, 2048, 2048), (512, 1024, 2048), (512, 6144, 2048),
                                    (512, 2048, 6144), (130, 2048, 2048), (2048, 256, 2048), (77, 300, 1024)])
 def test_linear_prefill_tensor_core_bit_exact(qvl, cuda, M, N, K):
     """M >= 16 with per-row scales runs the tcgen05 kind::i8 GEMM (hi/lo split
