@@ -397,6 +397,70 @@ def run_prefill_gemm(args):
         dist.destroy_process_group()
 
 
+def run_prefill(args):
+    """Prompt prefill (TTFT) of the text decoder: a 452-token prompt as one
+    M=452 pass (tensor-core GEMMs, causal attention), graph-captured.  value =
+    prompt tokens/s; the reference feeds prompts one token at a time."""
+    import torch
+    import torch.distributed as dist
+    import_qvl()
+    import qvl_b200.decoder as D
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = D.TextConfig()
+    T = PROMPT_CTX
+    w = D.TextWeights.random(cfg, seed=rank, device=dev)
+    dec = D.TextDecoder(w, max_batch=1, max_ctx=T + 8, device=dev)
+    prompt = torch.randint(0, 151643, (T,), dtype=torch.int32, device=dev,
+                           generator=torch.Generator(device=dev).manual_seed(rank))
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        dec.prefill(prompt)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dec.prefill(prompt)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ttft_ms = ms / args.steps
+    if rank == 0:
+        cpu = None
+        if args.cpu_seconds > 0:
+            del dec, g
+            torch.cuda.empty_cache()
+            tps, n, dt = cpu_decode_rate(args, seconds=args.cpu_seconds)
+            cpu = {"value": round(tps, 3), "unit": "prompt tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"{n} prompt tokens fed one at a time as the reference does ({dt * 1e3:.1f} ms each)"}
+        print(json.dumps({
+            "metric": "prefill_tokens_per_s", "value": round(T * ws * args.steps / (ms / 1e3), 1),
+            "unit": "prompt tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ttft_ms, "ttft_ms": ttft_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic (random ids, random-init weights)",
+            "config": {"workload": f"qwen3vl2b_text_prefill_T{T}", "order": "M=T tensor-core products (reference M>1 order)"},
+            "clocks": clk.summary(), "cpu_baseline": cpu,
+        }))
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -549,7 +613,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill_gemm"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_gemm"])
     ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -559,6 +623,8 @@ def main():
         run_reference(args)
     elif args.workload == "prefill_gemm":
         run_prefill_gemm(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)
 

@@ -258,6 +258,64 @@ class TextDecoder:
                     inplace_form=True)
         linear_batched(qx, qx_s, [(t["embed"], t["embed_s"])], [self.logits[:B]], ws)
 
+    def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0):
+        """Prompt of T tokens of request `seq` at positions start..start+T-1 as
+        one M=T pass: every linear is one tensor-core product (the reference's
+        M>1 order), attention is causal over the paged cache (query t sees
+        positions <= start+t).  Leaves the last token's logits and greedy id in
+        self.logits[seq] / self.tokens[seq] and self.positions[seq] = start+T.
+        The reference has no batched prefill: it feeds the prompt one token at
+        a time (model/src/utils.cpp:143-160); per token the arithmetic is the
+        same up to the GEMM order."""
+        cfg, t = self.cfg, self.w.t
+        T = tokens.numel()
+        H, I, D, ng, eps = cfg.hidden, cfg.intermediate, cfg.head_dim, cfg.norm_group, cfg.eps
+        dev = self.device
+        pf = getattr(self, "_pf", None)
+        if pf is None or pf["T"] < T:
+            f32, i16 = torch.float32, torch.int16
+            pf = dict(T=T, x=torch.zeros((T, H), dtype=f32, device=dev), q16=torch.zeros((T, I), dtype=i16, device=dev),
+                      qh=torch.zeros((T, H), dtype=i16, device=dev),
+                      qs=torch.zeros((T, 1), dtype=f32, device=dev), q=torch.zeros((T, cfg.heads * D), dtype=f32, device=dev),
+                      k=torch.zeros((T, cfg.kv_heads * D), dtype=f32, device=dev),
+                      v=torch.zeros((T, cfg.kv_heads * D), dtype=f32, device=dev),
+                      att=torch.zeros((T, cfg.heads * D), dtype=f32, device=dev),
+                      gate=torch.zeros((T, I), dtype=f32, device=dev), up=torch.zeros((T, I), dtype=f32, device=dev),
+                      logits=torch.zeros((1, cfg.vocab), dtype=f32, device=dev),
+                      seq=torch.zeros(T, dtype=torch.int32, device=dev),
+                      pos=torch.zeros(T, dtype=torch.int32, device=dev), ws=Workspace(dev))
+            pf["ws"].get(load_library().qvl_linear_q16_i8_batched_workspace_bytes(T, I))
+            self._pf = pf
+        x, q16, qs = pf["x"][:T], pf["q16"][:T], pf["qs"][:T]
+        qh = pf["qh"][:T]
+        pf["seq"][:T].fill_(seq)
+        torch.arange(start, start + T, dtype=torch.int32, device=dev, out=pf["pos"][:T])
+        sq, ps = pf["seq"][:T], pf["pos"][:T]
+        ws = pf["ws"]
+        embedding_lookup_i8(t["embed"], t["embed_s"], tokens.to(torch.int32), x)
+        for l in range(cfg.layers):
+            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
+            linear_batched(qh, qs, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
+                           [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
+            qknorm_rope_kv_append(pf["q"][:T], pf["k"][:T], pf["v"][:T], self.kv[l], sq, ps, self.rope_cos,
+                                  self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
+                                  t["k_norm_s"][l], ng, eps)
+            attention(pf["q"][:T], self.kv[l], sq, ps, self.max_ctx, out=pf["att"][:T], workspace=ws)
+            _quantize_into(pf["att"][:T], qh, qs)
+            linear_batched(qh, qs, [(t["wo"][l], t["wo_s"][l])], [x], ws, semantics=SEM_TILED | SEM_ACCUMULATE)
+            rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
+            linear_batched(qh, qs, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
+                           [pf["gate"][:T], pf["up"][:T]], ws, swiglu_pair=True, up_scratch=pf["up"][:T])
+            _quantize_into(pf["gate"][:T], q16, qs)
+            linear_batched(q16, qs, [(t["wd"][l], t["wd_s"][l])], [x], ws, semantics=SEM_TILED | SEM_ACCUMULATE)
+        last = x[T - 1:T]
+        rms_norm_i8(last, t["final_norm"], t["final_norm_s"], ng, eps, out=last, q=qh[:1], q_scales=qs[:1],
+                    quant_group=H, inplace_form=True)
+        linear_q16(qh[:1], qs[:1], t["embed"], t["embed_s"], H, C=pf["logits"], semantics=SEM_LANE8)
+        self.logits[seq].copy_(pf["logits"][0])
+        greedy_decode(pf["logits"], out=self.tokens[seq:seq + 1])
+        self.positions[seq:seq + 1].fill_(start + T)
+
     # launches of our kernels per step (attention = 3 kernels)
     def kernels_per_step(self):
         return 1 + self.cfg.layers * (1 + 1 + 1 + 3 + 1 + 1 + 1 + 1 + 1 + 1) + 1 + 1 + 1

@@ -89,3 +89,31 @@ def test_decode_batch_tensor_core_order(qvl, cuda):
         err = np.abs(got_logits[b] - ref_logits).max() / np.abs(ref_logits).max()
         assert err < 1e-3, (b, err)
         assert got_tok[b] == ref_tok, b
+
+
+def test_prefill_matches_token_by_token(qvl, cuda):
+    """Batched prefill (one M=T tensor-core pass, causal attention) against
+    the CPU decoder fed the prompt one token at a time in the same (M>1)
+    GEMM order: last-token logits within 1e-3, same greedy token, and the KV
+    cache it leaves behind within fp16 rounding of the CPU cache."""
+    import qvl_b200.decoder as D
+    cfg = _small_cfg(D, layers=1)
+    w = D.TextWeights.random(cfg, seed=21, device=cuda)
+    T = 40
+    dec = D.TextDecoder(w, max_batch=1, max_ctx=64, device=cuda)
+    prompt = torch.tensor([(7 * i + 3) % cfg.vocab for i in range(T)], dtype=torch.int32, device=cuda)
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    wn = w.numpy()
+    cos, sin = dec.rope_cos.cpu().numpy(), dec.rope_sin.cpu().numpy()
+    c = CpuDecoder(cfg, wn, 64, cos, sin, order="tiled")
+    for p in range(T):
+        ref_logits, ref_tok = c.step(int(prompt[p]), p)
+    got = dec.logits[0].cpu().numpy()
+    err = np.abs(got - ref_logits).max() / np.abs(ref_logits).max()
+    assert err < 1e-3, err
+    assert int(dec.tokens[0]) == ref_tok
+    assert int(dec.positions[0]) == T
+    pt = torch.from_numpy(dec.kv[0].page_table[0].cpu().numpy()).long().to(cuda)
+    kk = dec.kv[0].k[pt].float().cpu().numpy().transpose(1, 0, 2, 3).reshape(cfg.kv_heads, -1, cfg.head_dim)[:, :T]
+    assert np.abs(kk - c.kc[0][:, :T]).max() <= 2e-3 * np.abs(c.kc[0][:, :T]).max()
