@@ -559,8 +559,8 @@ def run_ours(args):
     if dec.use_tc:   # rmsnorm, split+3 GEMMs, rope, attention, quantize, split+GEMM, rmsnorm,
         # split+2 GEMMs+swiglu, quantize, split+GEMM
         per_layer, head = 1 + 4 + 1 + attn_k + 1 + 2 + 1 + 4 + 1 + 2, 1 + 1 + 2 + 1
-    elif B == 1:  # qkv, rope, attention, quantize, o(+norm tail), gate/up(+quant tail), down(+norm tail)
-        per_layer, head = 6 + attn_k, 1 + 1 + 1 + 1  # embedding, first rmsnorm, LM head, argmax
+    elif B == 1:  # qkv, rope, attention(+quantise tail), o(+norm tail), gate/up(+quant tail), down(+norm tail)
+        per_layer, head = 5 + (1 if attn_k == 1 else 4), 1 + 1 + 1 + 1  # embedding, first rmsnorm, LM head, argmax
     elif B <= 4:  # fast GEMV without the fused tails
         per_layer, head = 9 + attn_k, 1 + 2 + 1
     else:        # 8-row GEMV tiles, separate norms / swiglu

@@ -214,6 +214,17 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
                          const qvl_attn_dims *dims, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* qvl_attention_decode followed by the activation quantisation of each
+ * output row (one scale per row, the o_proj input): q_out int16 [nq, NH*D],
+ * q_out_scales fp32 [nq].  Fused into the attention launch when it runs as
+ * one launch; `counter` is a device int that must be 0 before the first call
+ * and is left 0. */
+int qvl_attention_decode_q16(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                             const int32_t *page_table, const int32_t *seq_ids, const int32_t *positions,
+                             size_t nq, int max_ctx, float *out, int16_t *q_out, float *q_out_scales,
+                             int *counter, const qvl_attn_dims *dims, void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 /* QK-norm + RoPE + KV append in one launch: rms_norm_inplace of every q and
  * k head with the layer's INT8 q_norm / k_norm weights (model/src/forward.cpp:
  * 531-538; layers/src/text_layer.cpp:234-272), then qvl_rope_kv_append.

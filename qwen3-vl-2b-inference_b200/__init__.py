@@ -45,6 +45,7 @@ EXPORTED = (
     "qvl_qknorm_rope_kv_append", "qvl_rms_norm_i8", "qvl_embedding_lookup_i8",
     "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
     "qvl_linear_q16_i8_tail", "qvl_linear_q16_i8_batched", "qvl_linear_q16_i8_batched_workspace_bytes",
+    "qvl_attention_decode_q16",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -106,6 +107,7 @@ def load_library(path: str = LIB_PATH):
     L.qvl_linear_q16_i8_batched_workspace_bytes.restype = _Z
     L.qvl_linear_q16_i8_batched_workspace_bytes.argtypes = [_Z, _Z]
     L.qvl_linear_q16_i8_batched.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _I, _I, _P, _P, _Z, _P]
+    L.qvl_attention_decode_q16.argtypes = [_P] * 6 + [_Z, _I, _P, _P, _P, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
     L.qvl_linear_q16_i8_multi.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _Z, _I, _P]
     _lib = L
     return L
@@ -376,3 +378,16 @@ def linear_batched(q, q_scales, mats, outs, workspace, semantics=SEM_TILED, swig
                                        int(swiglu_pair), _ptr(up_scratch), _ptr(ws), ws.numel(), _stream(stream)),
            "linear_batched")
     return outs
+
+
+def attention_q16(q, kv: PagedKV, seq_ids, positions, max_ctx, out, q_out, q_out_scales, counter,
+                  workspace=None, stream=None):
+    """attention + per-row quantisation of its output (fused when single-launch)."""
+    nq = q.shape[0]
+    L = load_library()
+    ws = _ws(workspace, q.device).get(L.qvl_attention_workspace_bytes(nq, max_ctx, ctypes.byref(kv.dims)))
+    _check(L.qvl_attention_decode_q16(_ptr(q), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table),
+                                      _ptr(seq_ids), _ptr(positions), nq, max_ctx, _ptr(out), _ptr(q_out),
+                                      _ptr(q_out_scales), _ptr(counter), ctypes.byref(kv.dims), _ptr(ws),
+                                      ws.numel(), _stream(stream)), "attention_q16")
+    return out

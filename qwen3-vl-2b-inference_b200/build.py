@@ -20,8 +20,11 @@ CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "lib")
 OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(LIBDIR, "libqvl_b200.so")
+SHIM = os.path.join(LIBDIR, "libqvl_b200_linear_shim.so")
+SHIM_SRC = os.path.join(PKG, "host", "linear_shim.cpp")
 
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
+CUDA_HOME = os.path.dirname(os.path.dirname(os.path.realpath(NVCC)))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include")]
@@ -64,6 +67,15 @@ def build(verbose: bool = False, ptxas_v: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stdout + r.stderr)
+    # C++ host shim with the reference's linear() signature (links the library)
+    if not os.path.exists(SHIM) or os.path.getmtime(SHIM) < max(os.path.getmtime(SHIM_SRC), os.path.getmtime(LIB)):
+        cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-o", SHIM, SHIM_SRC,
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(CUDA_HOME, "include"),
+               "-L" + LIBDIR, "-lqvl_b200", "-Wl,-rpath,$ORIGIN",
+               "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcudart"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("shim build failed:\n" + r.stdout + r.stderr)
     return LIB
 
 

@@ -22,6 +22,7 @@
 #include <cfloat>
 #include "common.cuh"
 #include "attention.cuh"
+#include "tail.cuh"
 #include <cooperative_groups.h>
 namespace cg = cooperative_groups;
 
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(kClusterThreads)
 attn_cluster_kernel(const float *__restrict q, const uint16_t *__restrict k_pages,
                     const uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
                     const int32_t *__restrict seq_ids, const int32_t *__restrict positions, int max_ctx,
-                    float *__restrict out, Dims d) {
+                    float *__restrict out, Dims d, RowTail tail) {
     extern __shared__ __align__(16) float sp[];          // [KVM][kSliceMax] scores / probabilities
     __shared__ float accs[16][KVM][kD + 4];              // per token-lane partials, then [0] = CTA partial
     __shared__ float redf[KVM][kClusterThreads / 32];
@@ -552,6 +553,9 @@ attn_cluster_kernel(const float *__restrict q, const uint16_t *__restrict k_page
         }
     }
     cluster.sync();                                       // keep shared memory alive for rank 0's reads
+    // Optional fused quantisation of the attention output rows (the o_proj
+    // input): the last rank-0 CTA to finish quantises every row.
+    if (tail.counter && rank == 0) run_row_tail(tail, reinterpret_cast<unsigned char *>(sp));
 }
 
 // ---------------------------------------------------------------- host side
@@ -622,8 +626,14 @@ cudaError_t launch_attn_t(const AttnArgs &a, const AttnScratch &s, char *ws, cud
         attr[1].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
+        RowTail tail = {};
+        if (a.q_out) {
+            tail.counter = a.counter; tail.x = a.out; tail.q = a.q_out; tail.qs = a.q_out_scales;
+            tail.qg = a.NH * kD; tail.H = a.NH * kD; tail.rows = (int)a.nq;
+            tail.participants = (int)a.nq * a.NKV;   // rank-0 CTAs of every cluster
+        }
         return cudaLaunchKernelEx(&cfg, kern, a.q, a.k_pages, a.v_pages, a.page_table, a.seq_ids, a.positions,
-                                  a.max_ctx, a.out, d);
+                                  a.max_ctx, a.out, d, tail);
     }
     float *scores = reinterpret_cast<float *>(ws + s.scores_off);
     float *cmax = reinterpret_cast<float *>(ws + s.cmax_off);

@@ -13,6 +13,11 @@ struct AttnArgs {
     int max_ctx;
     float *out;
     int NH, NKV, P, maxp, max_pos;
+    // optional quantisation of `out` rows (per-row group) for the next linear;
+    // honoured by the single-launch cluster path, otherwise done separately
+    int16_t *q_out;
+    float *q_out_scales;
+    int *counter;
 };
 
 // Optional per-layer QK-norm: INT8 weights [D] with fp32 group scales.

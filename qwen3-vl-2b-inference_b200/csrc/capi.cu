@@ -476,12 +476,45 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
     if (nq == 0) return QVL_OK;
     const size_t need = qvl_attention_workspace_bytes(nq, max_ctx, dims);
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
-    qvl::AttnArgs a;
+    qvl::AttnArgs a = {};
     a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
     a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
     a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
     a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
     QVL_CUDA_TRY(qvl::launch_attention(a, workspace, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_attention_decode_q16(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                             const int32_t *page_table, const int32_t *seq_ids, const int32_t *positions,
+                             size_t nq, int max_ctx, float *out, int16_t *q_out, float *q_out_scales,
+                             int *counter, const qvl_attn_dims *dims, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !k_pages || !v_pages || !page_table || !seq_ids || !positions || !out || !q_out ||
+        !q_out_scales || !counter)
+        return QVL_ERR_INVALID;
+    if (max_ctx <= 0) return QVL_ERR_INVALID;
+    if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(q, 16) || !aligned(out, 16)) return QVL_ERR_INVALID;
+    if (nq == 0) return QVL_OK;
+    const size_t need = qvl_attention_workspace_bytes(nq, max_ctx, dims);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    qvl::AttnArgs a = {};
+    a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
+    a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    const bool fused = qvl::attn_use_cluster(nq, max_ctx, a.NKV);
+    if (fused) {
+        a.q_out = q_out; a.q_out_scales = q_out_scales; a.counter = counter;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    QVL_CUDA_TRY(qvl::launch_attention(a, workspace, st));
+    if (!fused) {
+        const int H = dims->num_heads * dims->head_dim;
+        QVL_CUDA_TRY(qvl::launch_quantize_rows(out, q_out, q_out_scales, (int)nq, H, H, st));
+    }
     return QVL_OK;
 }
 

@@ -101,6 +101,7 @@ struct RowTail {
     int qg;
     int H;
     int rows;
+    int participants;          // CTAs that call run_row_tail (0: the whole grid)
 };
 
 // Bytes of dynamic shared memory the tail needs (the normalised row needs a
@@ -115,7 +116,7 @@ __device__ __forceinline__ void run_row_tail(const RowTail &t, unsigned char *sm
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();   // this CTA's outputs are visible before it is counted
-        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        const unsigned total = t.participants > 0 ? (unsigned)t.participants : gridDim.x * gridDim.y * gridDim.z;
         is_last = (atomicAdd(t.counter, 1) == (int)total - 1);
     }
     __syncthreads();

@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Workspace, attention, embedding_lookup_i8,
-               gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
+               attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
                qknorm_rope_kv_append, rms_norm_i8)
 from . import load_library
 
@@ -195,8 +195,12 @@ class TextDecoder:
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
-            attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
-            _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
+            if self.fuse_tails:
+                attention_q16(self.q[:B], self.kv[l], seq, pos, self.max_ctx, self.att[:B], self.qa[:B],
+                              self.qa_s[:B], self.counters[3], workspace=self.ws)
+            else:
+                attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+                _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
             if self.fuse_tails:
                 # o_proj + residual, then post-attention rms_norm -> gate/up input, one launch
                 linear_tail(self.qa[:B], self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], H, self.counters[0],

@@ -248,3 +248,26 @@ def test_linear_prefill_lm_head_rows(qvl, cuda):
     y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=False).cpu().numpy()
     ref = oracle.linear_i8(x[:4], w, ws, 2048, oracle.TILED)
     np.testing.assert_array_equal(y[:4], ref)
+
+
+@pytest.mark.parametrize("ctxs", [[300], [1, 700], [9000]])
+def test_attention_with_fused_quantisation(qvl, cuda, ctxs):
+    """attention_q16 == attention followed by quantize_rows (bit-exact),
+    on the single-launch path and on the split-K path."""
+    kv, _, q, kn, vn, cos, sin = _attn_setup(qvl, cuda, ctxs, seed=3)
+    B = len(ctxs)
+    qd = dev(q, cuda)
+    seq = torch.arange(B, dtype=torch.int32, device=cuda)
+    pos = torch.tensor([c - 1 for c in ctxs], dtype=torch.int32, device=cuda)
+    qvl.rope_kv_append(qd, dev(kn, cuda), dev(vn, cuda), kv, seq, pos, dev(cos, cuda), dev(sin, cuda))
+    out = torch.empty_like(qd)
+    q16 = torch.empty((B, NH * D), dtype=torch.int16, device=cuda)
+    s16 = torch.empty((B, 1), dtype=torch.float32, device=cuda)
+    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for _ in range(2):
+        qvl.attention_q16(qd, kv, seq, pos, max(ctxs), out, q16, s16, counter)
+    ref = qvl.attention(qd, kv, seq, pos, max(ctxs))
+    rq, rs = qvl.quantize_rows(ref.view(B, -1), NH * D)
+    assert torch.equal(out, ref)
+    assert torch.equal(q16, rq) and torch.equal(s16, rs)
+    assert int(counter.item()) == 0
