@@ -62,6 +62,8 @@ LINEAR = [
     (8, 2048, 2048, 2048),
     (13, 300, 2048, 512),    # ragged row tile (8 + 5)
     (1, 17, 512, 512),       # odd N
+    (4, 512, 1024, 64),      # generic kernel, TILED, 4-lane segments
+    (2, 256, 512, 32),       # generic kernel, TILED, 2-lane segments
 ]
 
 
