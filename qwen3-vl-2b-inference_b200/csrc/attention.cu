@@ -73,6 +73,11 @@ __global__ void rope_append_kernel(float *__restrict q, const float *__restrict 
     extern __shared__ __align__(16) float hs[];
     __shared__ float red[64 * 8];
     __shared__ float invh[64];
+    // constant operands first (QK-norm weights): into L2 before the wait
+    if (nrm.q_w && threadIdx.x < 4) {
+        const void *p[4] = {nrm.q_w, nrm.q_s, nrm.k_w, nrm.k_s};
+        prefetch_l2(p[threadIdx.x]);
+    }
     pdl_launch_dependents();
     pdl_wait();
     const int i = blockIdx.x;

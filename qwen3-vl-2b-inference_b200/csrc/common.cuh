@@ -69,6 +69,10 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
     return r;
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue (weight prefetch) while this one finishes, and wait for the
 // previous kernel's results before touching them.

@@ -80,6 +80,12 @@ gemv_i8_fast_kernel(const int16_t *__restrict q, const float *__restrict qs, Gem
         sdst[1] = (lane + 32 < G) ? __ldg(ws + lane + 32) : 0.0f;
     };
     if (n < N) issue(n, wr, wsr);
+    // the fused tail's constant operands (norm weight row and its scales) are
+    // pulled into L2 now, off the serial path of the last CTA
+    if (tail.counter && tail.wq && blockIdx.x == 0) {
+        for (int i = threadIdx.x * 128; i < tail.H; i += kThreads * 128) prefetch_l2(tail.wq + i);
+        if (threadIdx.x == 0) prefetch_l2(tail.ws);
+    }
 
     pdl_launch_dependents();
     pdl_wait();
