@@ -475,7 +475,8 @@ def run_ours(args):
     B = args.batch
     max_ctx = PROMPT_CTX + args.warmup + args.steps + 8
     w = D.TextWeights.random(cfg, seed=rank, device=dev)
-    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev)
+    persistent = args.engine == "persistent" or (args.engine == "auto" and B == 1 and max_ctx <= 8192)
+    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev, persistent=persistent)
     D.fill_kv_random(dec, PROMPT_CTX, seed=rank)
     dec.tokens.copy_(torch.arange(B, dtype=torch.int32, device=dev) * 7919 % cfg.vocab)
     stream = torch.cuda.Stream(dev)
@@ -567,9 +568,30 @@ def run_ours(args):
         tiles = (B + 7) // 8
         per_layer, head = 5 + attn_k + 7 * tiles, 1 + 1 + tiles + 1
     launches = args.steps * (cfg.layers * per_layer + head)
+    if persistent:
+        launches = args.steps * dec.kernels_per_step()
+        aborted = qvl.text_decode_aborted(dec.pws)
+        if aborted:
+            raise RuntimeError("persistent decode: a grid barrier wait timed out")
     gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = load_peaks()
+        gemv_roof = {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gemv_gbs / peak, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic("gemv_i8_decode"), "kernel": "gemv_i8 (decode GEMVs)",
+                     "algorithmic_bytes_per_launch": round(gemv_bytes_per_launch),
+                     "avg_launch_us": round(gemv_s_per_launch * 1e6, 3)}
+        if persistent:
+            # one launch per token: its algorithmic bytes are the step's
+            # weights plus the KV rows read at the mean context
+            roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind,
+                        "traffic": profile_traffic("decode_persistent"),
+                        "kernel": "decode_persistent (whole token, one cooperative launch)",
+                        "algorithmic_bytes_per_launch": round(w_bytes + kv_bytes),
+                        "avg_launch_us": round(ms_step * 1e3, 3), "gemv_chain": gemv_roof}
+        else:
+            roofline = gemv_roof
         cpu = None
         if args.cpu_seconds > 0:
             del dec, g, ge
@@ -586,13 +608,10 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int16xint8->int32", "data": "synthetic (random-init int8 weights, seed = rank)",
             "config": dict(decode_config(args, ws),
+                           engine="persistent (one launch per token)" if persistent else "launch chain",
                            batch_order="tiled (M=B tcgen05, reference M>1 order)" if tc_mode
                            else "lane8 (each request in the reference M=1 order)"),
-            "roofline": {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gemv_gbs / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profile_traffic("gemv_i8_decode"), "kernel": "gemv_i8 (decode GEMVs)",
-                         "algorithmic_bytes_per_launch": round(gemv_bytes_per_launch),
-                         "avg_launch_us": round(gemv_s_per_launch * 1e6, 3)},
+            "roofline": roofline,
             "step_hbm_gbs": round(step_gbs, 1),
             "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B},
@@ -614,6 +633,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_gemm"])
+    ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
+                    help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")
     ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

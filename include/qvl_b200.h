@@ -284,6 +284,54 @@ int qvl_attention_decode_static(const float *q, const uint16_t *k_pages,
  * -FLT_MAX; NaN never wins; all-NaN/-inf rows give 0). */
 int qvl_argmax_rows(const float *logits, int32_t *idx, size_t rows, size_t n, void *stream);
 
+/* ---- one whole decode token in one launch (batch 1) ---------------------
+ * Replaces, for one request, the per-token text decoder of forward_text
+ * (model/src/forward.cpp:458-720) followed by greedy_decode
+ * (tokenizer/src/utils.cpp:34-44): embedding lookup of *token, 28 x (input
+ * rms_norm, q/k/v linear, q/k rms_norm_inplace + RoPE, KV append, attention,
+ * o_proj + residual, post rms_norm, gate/up + SwiGLU, down + residual), final
+ * rms_norm_inplace, LM head (tied embedding) into `logits`, greedy token into
+ * *token, *pos += 1.  `token` and `pos` stay on the device, so consecutive
+ * calls (or a captured graph of them) decode without host round trips.
+ *
+ * One cooperative kernel: every CTA stays resident for the whole token and
+ * the phases meet at a grid barrier whose waits are bounded (2 s); a timeout
+ * sets an abort word in the workspace (qvl_text_decode_abort_flag) and every
+ * CTA leaves.  Arithmetic per operation is that of the separate entry points
+ * with QVL_SEM_LANE8 (M=1 GEMV order); the attention splits each context into
+ * 16 slices, so its fp32 partial sums are grouped differently.
+ *
+ * Supported: Qwen3-VL-2B text dims (hidden 2048, intermediate 6144, 16 heads,
+ * 8 KV heads, head_dim 128), per-output-row INT8 linear weights (group_size
+ * == K), max_ctx <= 8192.  Weights are stacked over layers: w_q [L, 2048,
+ * 2048] etc., s_q [L, 2048]; norm weights int8 [L, n] with fp32 group scales
+ * [L, n / norm_group].  KV pages [L][pages, 8, page_size, 128] fp16, layer l at
+ * l * kv_layer_stride elements; page_table [ceil(max_ctx / page_size)].
+ * workspace: qvl_text_decode_workspace_bytes() bytes, ZERO-FILLED before the
+ * first call and then kept (it holds the barrier words); calls sharing one
+ * workspace must be ordered on one stream. */
+typedef struct {
+    const int8_t *w_q, *w_k, *w_v, *w_o, *w_gate, *w_up, *w_down;
+    const float *s_q, *s_k, *s_v, *s_o, *s_gate, *s_up, *s_down;
+    const int8_t *in_norm, *post_norm, *q_norm, *k_norm;
+    const float *in_norm_s, *post_norm_s, *q_norm_s, *k_norm_s;
+    const int8_t *final_norm;
+    const float *final_norm_s;
+    const int8_t *embed;          /* [vocab, hidden], also the LM head */
+    const float *embed_s;         /* [vocab] */
+    int layers, vocab, hidden, intermediate, heads, kv_heads, head_dim, norm_group;
+    float eps;
+} qvl_text_weights;
+
+size_t qvl_text_decode_workspace_bytes(void);
+int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int32_t *token,
+                         int32_t *pos, uint16_t *k_pages, uint16_t *v_pages, long kv_layer_stride,
+                         const int32_t *page_table, int page_size, const float *rope_cos,
+                         const float *rope_sin, int max_ctx, void *workspace,
+                         size_t workspace_bytes, void *stream);
+/* Device address of the abort word inside `workspace` (int, 0 = healthy). */
+int *qvl_text_decode_abort_flag(void *workspace);
+
 #ifdef __cplusplus
 }
 #endif

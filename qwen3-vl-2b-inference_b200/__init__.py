@@ -45,7 +45,8 @@ EXPORTED = (
     "qvl_qknorm_rope_kv_append", "qvl_rms_norm_i8", "qvl_embedding_lookup_i8",
     "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
     "qvl_linear_q16_i8_tail", "qvl_linear_q16_i8_batched", "qvl_linear_q16_i8_batched_workspace_bytes",
-    "qvl_attention_decode_q16",
+    "qvl_attention_decode_q16", "qvl_text_decode_workspace_bytes", "qvl_text_decode_step",
+    "qvl_text_decode_abort_flag",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -65,6 +66,17 @@ class RowTail(ctypes.Structure):
                 ("norm_group", ctypes.c_size_t), ("eps", ctypes.c_float), ("inplace_form", ctypes.c_int),
                 ("norm_out", ctypes.c_void_p), ("q", ctypes.c_void_p), ("q_scales", ctypes.c_void_p),
                 ("quant_group", ctypes.c_size_t)]
+
+
+class TextWeightsC(ctypes.Structure):
+    """qvl_text_weights: stacked device pointers of the text decoder."""
+    _fields_ = ([(n, ctypes.c_void_p) for n in (
+        "w_q", "w_k", "w_v", "w_o", "w_gate", "w_up", "w_down", "s_q", "s_k", "s_v", "s_o", "s_gate", "s_up",
+        "s_down", "in_norm", "post_norm", "q_norm", "k_norm", "in_norm_s", "post_norm_s", "q_norm_s",
+        "k_norm_s", "final_norm", "final_norm_s", "embed", "embed_s")]
+        + [(n, ctypes.c_int) for n in ("layers", "vocab", "hidden", "intermediate", "heads", "kv_heads",
+                                       "head_dim", "norm_group")]
+        + [("eps", ctypes.c_float)])
 
 
 _P, _Z, _I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
@@ -109,6 +121,12 @@ def load_library(path: str = LIB_PATH):
     L.qvl_linear_q16_i8_batched.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _I, _I, _P, _P, _Z, _P]
     L.qvl_attention_decode_q16.argtypes = [_P] * 6 + [_Z, _I, _P, _P, _P, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
     L.qvl_linear_q16_i8_multi.argtypes = [_P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _Z, _I, _P]
+    L.qvl_text_decode_workspace_bytes.restype = _Z
+    L.qvl_text_decode_workspace_bytes.argtypes = []
+    L.qvl_text_decode_step.argtypes = [ctypes.POINTER(TextWeightsC)] + [_P] * 6 + [ctypes.c_long, _P, _I, _P, _P,
+                                                                                _I, _P, _Z, _P]
+    L.qvl_text_decode_abort_flag.restype = _P
+    L.qvl_text_decode_abort_flag.argtypes = [_P]
     _lib = L
     return L
 
@@ -229,13 +247,17 @@ class PagedKV:
     [num_seqs, max_pages_per_seq] (identity-mapped unless given)."""
 
     def __init__(self, num_seqs, max_ctx, num_heads=16, num_kv_heads=8, head_dim=128,
-                 page_size=64, max_pos=None, device="cuda", page_table=None):
+                 page_size=64, max_pos=None, device="cuda", page_table=None, k=None, v=None):
+        """k, v: optional preallocated page tensors (e.g. one layer of a
+        stacked [layers, pages, ...] cache); zero-filled pages otherwise."""
         self.page_size = page_size
         self.maxp = (max_ctx + page_size - 1) // page_size
         num_pages = num_seqs * self.maxp
         shape = (num_pages, num_kv_heads, page_size, head_dim)
-        self.k = torch.zeros(shape, dtype=torch.float16, device=device)
-        self.v = torch.zeros(shape, dtype=torch.float16, device=device)
+        self.k = torch.zeros(shape, dtype=torch.float16, device=device) if k is None else k
+        self.v = torch.zeros(shape, dtype=torch.float16, device=device) if v is None else v
+        if tuple(self.k.shape) != shape or tuple(self.v.shape) != shape:
+            raise QvlError(f"KV pages must have shape {shape}")
         if page_table is None:
             page_table = torch.arange(num_pages, dtype=torch.int32, device=device).view(num_seqs, self.maxp)
         self.page_table = page_table.contiguous()
@@ -265,6 +287,47 @@ def attention(q, kv: PagedKV, seq_ids, positions, max_ctx, out=None, workspace=N
                                   ctypes.byref(kv.dims), _ptr(ws), ws.numel(), _stream(stream)),
            "attention")
     return out
+
+
+def text_weights_struct(t: dict, cfg) -> TextWeightsC:
+    """qvl_text_weights for the stacked weight dict of decoder.TextWeights
+    (the tensors must stay alive while the struct is used)."""
+    names = {"w_q": "wq", "w_k": "wk", "w_v": "wv", "w_o": "wo", "w_gate": "wg", "w_up": "wu", "w_down": "wd"}
+    w = TextWeightsC()
+    for f, n in names.items():
+        setattr(w, f, _ptr(t[n]))
+        setattr(w, "s" + f[1:], _ptr(t[n + "_s"]))
+    for n in ("in_norm", "post_norm", "q_norm", "k_norm", "final_norm", "embed"):
+        setattr(w, n, _ptr(t[n]))
+        setattr(w, n + "_s", _ptr(t[n + "_s"]))
+    w.layers, w.vocab, w.hidden, w.intermediate = cfg.layers, cfg.vocab, cfg.hidden, cfg.intermediate
+    w.heads, w.kv_heads, w.head_dim, w.norm_group = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.norm_group
+    w.eps = cfg.eps
+    return w
+
+
+def text_decode_workspace(device) -> torch.Tensor:
+    """Zero-filled workspace for text_decode_step (keep it between calls)."""
+    n = load_library().qvl_text_decode_workspace_bytes()
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def text_decode_step(w: TextWeightsC, x, logits, token, pos, k_all, v_all, page_table, page_size, rope_cos,
+                     rope_sin, max_ctx, workspace, stream=None):
+    """One whole decode token of one request in one launch: reads token[0] and
+    pos[0], writes logits and x, replaces token[0] by the greedy token and
+    advances pos[0].  k_all / v_all: [layers, pages, NKV, page_size, D] fp16."""
+    layer_stride = k_all[0].numel()
+    _check(load_library().qvl_text_decode_step(
+        ctypes.byref(w), _ptr(x), _ptr(logits), _ptr(token), _ptr(pos), _ptr(k_all), _ptr(v_all), layer_stride,
+        _ptr(page_table), page_size, _ptr(rope_cos), _ptr(rope_sin), max_ctx, _ptr(workspace),
+        workspace.numel(), _stream(stream)), "text_decode_step")
+
+
+def text_decode_aborted(workspace) -> bool:
+    """True if a grid-barrier wait of text_decode_step timed out (synchronises)."""
+    off = load_library().qvl_text_decode_abort_flag(_ptr(workspace)) - workspace.data_ptr()
+    return bool(workspace[off:off + 4].view(torch.int32).item())
 
 
 def greedy_decode(logits: torch.Tensor, out=None, stream=None) -> torch.Tensor:

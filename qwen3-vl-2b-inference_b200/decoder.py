@@ -30,7 +30,7 @@ import torch
 
 from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Workspace, attention, embedding_lookup_i8,
                attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
-               qknorm_rope_kv_append, rms_norm_i8)
+               qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct)
 from . import load_library
 
 
@@ -107,12 +107,14 @@ class TextDecoder:
     """Batched decode over a paged FP16 KV cache (one sequence per request)."""
 
     def __init__(self, weights: TextWeights, max_batch: int, max_ctx: int, page_size: int = 64,
-                 device="cuda", batch_order: str = "auto"):
+                 device="cuda", batch_order: str = "auto", persistent: bool = False):
         """batch_order: "lane8" computes every request row in the reference's
         M=1 decode order (CUDA-core GEMV, each request bit-matches the
         reference run on it alone); "tiled" runs the batch as one M=B product
         on the tensor cores in the reference's M>1 order (what the reference's
-        linear() does for an M>1 call); "auto" = tiled for B >= 16."""
+        linear() does for an M>1 call); "auto" = tiled for B >= 16.
+        persistent: (max_batch 1 only) run each token as ONE cooperative
+        launch (qvl_text_decode_step) instead of ~6 launches per layer."""
         self.w = weights
         cfg = self.cfg = weights.cfg
         self.B = max_batch
@@ -138,8 +140,20 @@ class TextDecoder:
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(B, dtype=torch.int32, device=dev)
         self.seq_ids = torch.arange(B, dtype=torch.int32, device=dev)
-        self.kv = [PagedKV(B, max_ctx, cfg.heads, cfg.kv_heads, D, page_size, max_pos=max_ctx, device=dev)
-                   for _ in range(cfg.layers)]
+        # one stacked cache (uniform layer stride), viewed per layer
+        maxp = (max_ctx + page_size - 1) // page_size
+        kv_shape = (cfg.layers, B * maxp, cfg.kv_heads, page_size, D)
+        self.k_all = torch.zeros(kv_shape, dtype=torch.float16, device=dev)
+        self.v_all = torch.zeros(kv_shape, dtype=torch.float16, device=dev)
+        self.page_size = page_size
+        self.kv = [PagedKV(B, max_ctx, cfg.heads, cfg.kv_heads, D, page_size, max_pos=max_ctx, device=dev,
+                           k=self.k_all[l], v=self.v_all[l]) for l in range(cfg.layers)]
+        if persistent and max_batch != 1:
+            raise ValueError("persistent decode serves one request (max_batch 1)")
+        self.persistent = persistent
+        if persistent:
+            self.pw = text_weights_struct(weights.t, cfg)
+            self.pws = text_decode_workspace(dev)
         cos, sin = rope_table(max_ctx, D, cfg.rope_theta)
         self.set_rope_table(cos, sin)
         self.counters = torch.zeros(4, dtype=torch.int32, device=dev)   # fused-tail counters (stay 0)
@@ -174,6 +188,11 @@ class TextDecoder:
         tokens in self.tokens, and advances self.positions by one.  Only
         device work is issued (graph-capturable)."""
         B = B or self.B
+        if self.persistent:
+            text_decode_step(self.pw, self.x, self.logits, self.tokens, self.positions, self.k_all, self.v_all,
+                             self.kv[0].page_table, self.page_size, self.rope_cos, self.rope_sin, self.max_ctx,
+                             self.pws)
+            return
         cfg, t = self.cfg, self.w.t
         H, ng, eps = cfg.hidden, cfg.norm_group, cfg.eps
         x = self.x[:B]
@@ -322,6 +341,8 @@ class TextDecoder:
 
     # launches of our kernels per step (attention = 3 kernels)
     def kernels_per_step(self):
+        if self.persistent:
+            return 1
         return 1 + self.cfg.layers * (1 + 1 + 1 + 3 + 1 + 1 + 1 + 1 + 1 + 1) + 1 + 1 + 1
 
 

@@ -50,3 +50,32 @@ def test_unsupported_group_size_is_reported():
     fake = ctypes.c_void_p(256)   # never dereferenced: shape check fails first
     rc = L.qvl_linear_q16_i8(fake, fake, fake, fake, fake, 1, 16, 96 * 3, 96, 0, None)
     assert rc == 2
+
+
+def test_text_decode_step_validation_without_gpu():
+    """qvl_text_decode_step rejects bad arguments before any CUDA call."""
+    qvl = import_qvl()
+    L = qvl.load_library()
+    fake = 4096                      # aligned, never dereferenced
+    w = qvl.TextWeightsC()
+    for name, _ in qvl.TextWeightsC._fields_[:26]:
+        setattr(w, name, fake)
+    w.layers, w.vocab, w.hidden, w.intermediate = 2, 4096, 2048, 6144
+    w.heads, w.kv_heads, w.head_dim, w.norm_group, w.eps = 16, 8, 128, 128, 1e-6
+    ws_bytes = L.qvl_text_decode_workspace_bytes()
+    assert ws_bytes > 0
+
+    def call(max_ctx=64, ws=fake, nbytes=ws_bytes, stride=8192, weights=w):
+        return L.qvl_text_decode_step(ctypes.byref(weights), fake, fake, fake, fake, fake, fake, stride, fake, 64,
+                                      fake, fake, max_ctx, ws, nbytes, None)
+
+    assert call(max_ctx=8193) == 2            # context above 16 slices x 512
+    assert call(nbytes=ws_bytes - 1) == 4     # workspace too small
+    assert call(ws=fake + 16) == 4            # workspace not 256-byte aligned
+    assert call(stride=12) == 1               # layer stride breaks 16-byte KV rows
+    w.intermediate = 4096
+    assert call() == 2                        # other model dims are not compiled in
+    w.intermediate = 6144
+    w.w_q = None
+    assert call() == 1
+    assert L.qvl_text_decode_step(None, *([None] * 6), 0, None, 0, None, None, 0, None, 0, None) == 1
