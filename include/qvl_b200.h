@@ -303,7 +303,8 @@ int qvl_argmax_rows(const float *logits, int32_t *idx, size_t rows, size_t n, vo
  *
  * Supported: Qwen3-VL-2B text dims (hidden 2048, intermediate 6144, 16 heads,
  * 8 KV heads, head_dim 128), per-output-row INT8 linear weights (group_size
- * == K), max_ctx <= 8192.  Weights are stacked over layers: w_q [L, 2048,
+ * == K), vocab a multiple of 16, page_size a multiple of 16, max_ctx <= 8192;
+ * weight matrices and their scale arrays 16-byte aligned.  Weights are stacked over layers: w_q [L, 2048,
  * 2048] etc., s_q [L, 2048]; norm weights int8 [L, n] with fp32 group scales
  * [L, n / norm_group].  KV pages [L][pages, 8, page_size, 128] fp16, layer l at
  * l * kv_layer_stride elements; page_table [ceil(max_ctx / page_size)].
@@ -331,6 +332,10 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
                          size_t workspace_bytes, void *stream);
 /* Device address of the abort word inside `workspace` (int, 0 = healthy). */
 int *qvl_text_decode_abort_flag(void *workspace);
+/* Device address of the phase trace inside `workspace`: 256 uint64
+ * global-timer stamps (ns) of the last call -- [0] kernel start, [1 + i] the
+ * opening of grid barrier i (1 + 7 per layer + 1 barriers per token). */
+const uint64_t *qvl_text_decode_trace(const void *workspace);
 
 #ifdef __cplusplus
 }

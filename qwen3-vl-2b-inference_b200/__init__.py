@@ -29,6 +29,7 @@ from __future__ import annotations
 import ctypes
 import os
 
+import numpy as np
 import torch
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
@@ -46,7 +47,7 @@ EXPORTED = (
     "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
     "qvl_linear_q16_i8_tail", "qvl_linear_q16_i8_batched", "qvl_linear_q16_i8_batched_workspace_bytes",
     "qvl_attention_decode_q16", "qvl_text_decode_workspace_bytes", "qvl_text_decode_step",
-    "qvl_text_decode_abort_flag",
+    "qvl_text_decode_abort_flag", "qvl_text_decode_trace",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -127,6 +128,8 @@ def load_library(path: str = LIB_PATH):
                                                                                 _I, _P, _Z, _P]
     L.qvl_text_decode_abort_flag.restype = _P
     L.qvl_text_decode_abort_flag.argtypes = [_P]
+    L.qvl_text_decode_trace.restype = _P
+    L.qvl_text_decode_trace.argtypes = [_P]
     _lib = L
     return L
 
@@ -328,6 +331,13 @@ def text_decode_aborted(workspace) -> bool:
     """True if a grid-barrier wait of text_decode_step timed out (synchronises)."""
     off = load_library().qvl_text_decode_abort_flag(_ptr(workspace)) - workspace.data_ptr()
     return bool(workspace[off:off + 4].view(torch.int32).item())
+
+
+def text_decode_trace(workspace) -> np.ndarray:
+    """Phase timestamps (ns) of the last text_decode_step on this workspace:
+    [0] kernel start, [1 + i] opening of grid barrier i (synchronises)."""
+    off = load_library().qvl_text_decode_trace(_ptr(workspace)) - workspace.data_ptr()
+    return workspace[off:off + 1024 * 8].view(torch.int64).cpu().numpy()
 
 
 def greedy_decode(logits: torch.Tensor, out=None, stream=None) -> torch.Tensor:

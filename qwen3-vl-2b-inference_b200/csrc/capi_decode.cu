@@ -10,12 +10,13 @@ constexpr size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 // Workspace layout; the barrier words come first so that they keep their
 // place whatever the device's SM count.
 struct DecodeWs {
-    size_t bar, x_qkv, h, lmax, lsum, pacc, best_v, best_i, total;
+    size_t bar, trace, x_qkv, h, lmax, lsum, pacc, best_v, best_i, total;
 };
 constexpr DecodeWs decode_ws() {
     DecodeWs w{};
-    w.bar = 0;                                             // bar_count, bar_gen, abort
-    w.x_qkv = 256;
+    w.bar = 0;                                             // bar_count (u64), abort (int at +8)
+    w.trace = 256;
+    w.x_qkv = w.trace + qvl::kPersistTraceSlots * 8;
     w.h = w.x_qkv + al256((16 * 128 + 2 * 8 * 128) * 4);
     w.lmax = w.h + al256(6144 * 4);
     w.lsum = w.lmax + al256(16 * qvl::kPersistSlices * 4);
@@ -36,6 +37,12 @@ int *qvl_text_decode_abort_flag(void *workspace) {
     return workspace ? reinterpret_cast<int *>(static_cast<unsigned char *>(workspace) + 8) : nullptr;
 }
 
+const uint64_t *qvl_text_decode_trace(const void *workspace) {
+    return workspace ? reinterpret_cast<const uint64_t *>(static_cast<const unsigned char *>(workspace) +
+                                                          decode_ws().trace)
+                     : nullptr;
+}
+
 int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int32_t *token, int32_t *pos,
                          uint16_t *k_pages, uint16_t *v_pages, long kv_layer_stride, const int32_t *page_table,
                          int page_size, const float *rope_cos, const float *rope_sin, int max_ctx, void *workspace,
@@ -48,13 +55,14 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
                           w->final_norm_s, w->embed, w->embed_s};
     for (const void *p : ptrs)
         if (!p) return QVL_ERR_INVALID;
-    if (w->layers <= 0 || w->vocab <= 0 || page_size <= 0 || kv_layer_stride <= 0 || !(w->eps >= 0.0f))
+    if (w->layers <= 0 || w->vocab <= 0 || w->vocab % 16 || page_size < 16 || page_size % 16 || kv_layer_stride <= 0 || !(w->eps >= 0.0f))
         return QVL_ERR_INVALID;
-    if (w->norm_group <= 0 || w->head_dim % w->norm_group || w->hidden % w->norm_group) return QVL_ERR_INVALID;
+    if (w->norm_group < 16 || w->head_dim % w->norm_group || w->hidden % w->norm_group) return QVL_ERR_INVALID;
     if (!qvl::persist_supported(w->hidden, w->intermediate, w->heads, w->kv_heads, w->head_dim, max_ctx))
         return QVL_ERR_UNSUPPORTED;
-    // 16-byte loads of weight rows, KV rows and activations
+    // 16-byte copies of weight rows and their scales, 16-byte KV rows and activations
     const void *aligned[] = {w->w_q, w->w_k, w->w_v, w->w_o, w->w_gate, w->w_up, w->w_down, w->embed,
+                             w->s_q, w->s_k, w->s_v, w->s_o, w->s_gate, w->s_up, w->s_down, w->embed_s,
                              k_pages, v_pages, x};
     for (const void *p : aligned)
         if (reinterpret_cast<uintptr_t>(p) & 15) return QVL_ERR_INVALID;
@@ -98,9 +106,9 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
     ps.rope_cos = rope_cos;
     ps.rope_sin = rope_sin;
     ps.max_ctx = max_ctx;
-    ps.bar_count = reinterpret_cast<unsigned *>(ws);
-    ps.bar_gen = reinterpret_cast<unsigned *>(ws + 4);
+    ps.bar_count = reinterpret_cast<unsigned long long *>(ws);
     ps.abort_flag = reinterpret_cast<int *>(ws + 8);
+    ps.trace = reinterpret_cast<unsigned long long *>(ws + L.trace);
     QVL_CUDA_TRY(qvl::launch_decode_persistent(pw, ps, ctas, (cudaStream_t)stream));
     return QVL_OK;
 }

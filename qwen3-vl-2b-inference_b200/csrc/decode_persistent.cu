@@ -4,26 +4,38 @@
 //
 // Why: at batch 1 the step is a chain of small dependent operations (see
 // forward_text, model/src/forward.cpp:458-720); as separate launches each
-// costs >= 2.3 us of hand-off plus its own latency.  Here every CTA stays
-// resident and the phases are separated by a grid-wide barrier.  Small
-// row operations (RMSNorm + quantisation, attention combine + quantisation)
-// are computed redundantly by every CTA from L2 instead of by one CTA plus a
-// barrier; matrix rows are spread over all warps of the grid.
+// costs >= 2.3 us of hand-off plus its own latency, and the weight stream
+// stops at every hand-off.  Here every CTA stays resident, the phases are
+// separated by a grid-wide barrier, and the weights never wait for them:
+//
+//   * Weight stream.  Every weight row the token needs is known in advance.
+//     Each CTA owns a fixed list of 16-row blocks of every matrix (block
+//     u = blockIdx.x + j * gridDim.x) and streams them, in the order it will
+//     use them, through a ring of kStages 32 KB shared-memory stages with
+//     bulk asynchronous copies (cp.async.bulk, completion on an mbarrier, no
+//     multicast).  One thread keeps the ring full, so while the grid waits
+//     at a barrier or computes attention, the next matrices are already
+//     flowing from HBM.  Warp w computes row w of every stage.
+//   * Small row operations (RMSNorm + quantisation, attention combine +
+//     quantisation) are computed redundantly by every CTA from L2 instead
+//     of by one CTA plus another barrier.
 //
 // Arithmetic is the multi-kernel path's, operation by operation (M=1 GEMV
-// lane order, reference RMSNorm / quantisation / SwiGLU / RoPE / softmax
-// rules); only the attention's split of the context (16 slices per KV head)
-// changes fp32 summation order there.
+// lane order with exact int32 lane sums, reference RMSNorm / quantisation /
+// SwiGLU / RoPE / softmax rules); only the attention's split of the context
+// (16 slices per KV head) changes fp32 summation order there.
 //
-// Safety: every barrier wait is bounded by the global timer; a timeout sets
-// the abort flag, after which every CTA leaves at its next barrier.  The
-// launch is cooperative, so all CTAs are co-resident (the launch fails
-// instead of deadlocking if they cannot be).
+// Safety: every wait (grid barrier, mbarrier) is bounded by the global timer;
+// a timeout sets the abort flag, after which every CTA drains its own copies
+// in flight (bounded) and leaves at its next barrier.  The launch is
+// cooperative, so all CTAs are co-resident (the launch fails instead of
+// deadlocking if they cannot be).
 #include <cfloat>
 #include <climits>
 #include <cuda_fp16.h>
 #include "gemv_common.cuh"
 #include "tail.cuh"
+#include "tc_common.cuh"
 #include "decode_persistent.cuh"
 
 namespace qvl {
@@ -32,42 +44,83 @@ namespace {
 constexpr int kPThreads = 512;
 constexpr int kPWarps = kPThreads / 32;
 constexpr int H = 2048, I = 6144, NH = 16, NKV = 8, D = 128;
-constexpr int kSlices = 16;                    // attention context slices per KV head
+constexpr int kSlices = kPersistSlices;        // attention context slices per KV head
 constexpr int kSliceMax = 512;                 // tokens per slice (context <= 8192)
+constexpr int kMaxPages = kSlices * kSliceMax / 16;   // page table entries (page_size >= 16)
 constexpr unsigned long long kBarrierLimitNs = 2000000000ull;
+constexpr unsigned kTraceSlots = kPersistTraceSlots;
+
+// weight ring: a stage is 16 row segments of 2048 bytes, one per warp
+constexpr int kRows = kPWarps;
+constexpr int kSegBytes = 2048;
+constexpr int kStageBytes = kRows * kSegBytes;
+constexpr int kStages = 5;
+
+// dynamic shared memory: ring | q16 [I] int16 | xs [I] f32 | ts [H] f32 | sp [2][kSliceMax] f32 |
+// nrm_w [H] f32 | nrm_s [H / norm_group] f32 (norm_group >= 16)
+constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
+constexpr size_t kSmemBytes = kRingBytes + (size_t)I * 2 + (size_t)I * 4 + (size_t)H * 4 + 2 * (size_t)kSliceMax * 4 +
+                              (size_t)H * 4 + (size_t)H * 4 / 16;
+
+// matrices in stream order; units are 16-row blocks, subs the stages per unit
+enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_LM = 4, PH_DONE = 5 };
+__device__ __forceinline__ int ph_units(int ph, int vocab) {
+    return ph == PH_QKV ? (NH * D + 2 * NKV * D) / kRows
+         : ph == PH_O ? H / kRows
+         : ph == PH_GU ? I / kRows
+         : ph == PH_DOWN ? H / kRows
+         : vocab / kRows;
+}
+__device__ __forceinline__ int ph_subs(int ph) { return ph == PH_GU ? 2 : ph == PH_DOWN ? I / kSegBytes : 1; }
+// units u = blockIdx.x + j * gridDim.x below U
+__device__ __forceinline__ int cta_units(int U) {
+    return U > (int)blockIdx.x ? (U - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+}
 
 __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
     return *reinterpret_cast<const volatile unsigned *>(p);
 }
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
-// Grid barrier with a bounded wait.  Returns false once any CTA has aborted.
-__device__ __forceinline__ bool grid_sync(const PersistState &S, unsigned &gen) {
+// Grid barrier with a bounded wait.  The counter only grows (it is zero
+// when the workspace is cleared), so barrier k of a launch completes when
+// the arrivals reach the next multiple of gridDim.x: no reset, no second
+// word.  Release on arrival / acquire on the wait, each after / before a CTA
+// barrier (the CTA's writes are ordered by bar.sync, then published by the
+// release).  Returns false if the wait gave up or another CTA aborted.
+// CTA 0 records the time each barrier opens in S.trace[1 + k].
+__device__ __forceinline__ bool grid_sync(const PersistState &S, int &nsync) {
     __syncthreads();
     __shared__ int ok;
     if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned arrived = atomicAdd(S.bar_count, 1u) + 1u;
-        if (arrived == gridDim.x) {
-            atomicExch(S.bar_count, 0u);
-            __threadfence();
-            atomicExch(S.bar_gen, gen + 1u);
-        } else {
-            unsigned long long t0;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-            while (ld_volatile(S.bar_gen) == gen) {
-                if (ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag))) break;
-                unsigned long long t;
-                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-                if (t - t0 > kBarrierLimitNs) {
-                    atomicExch(S.abort_flag, 1);
-                    break;
+        unsigned long long old, v;
+        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.bar_count) : "memory");
+        const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+        int good = 1;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.bar_count) : "memory");
+        if (v < target) {
+            const unsigned long long t0 = global_ns();
+            for (unsigned it = 1;; ++it) {
+                asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.bar_count) : "memory");
+                if (v >= target) break;
+                if ((it & 15) == 0) {
+                    if (ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag))) { good = 0; break; }
+                    if (global_ns() - t0 > kBarrierLimitNs) {
+                        atomicExch(S.abort_flag, 1);
+                        good = 0;
+                        break;
+                    }
                 }
             }
         }
-        __threadfence();
-        ok = ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag)) == 0;
+        ok = good;
+        if (blockIdx.x == 0 && (unsigned)nsync + 1 < kTraceSlots) S.trace[nsync + 1] = global_ns();
     }
-    ++gen;
+    ++nsync;
     __syncthreads();
     return ok;
 }
@@ -82,40 +135,149 @@ __device__ __forceinline__ void h8f(const uint4 &v, float f[8]) {
     }
 }
 
-__device__ __forceinline__ size_t kv_off(const PersistState &S, int layer, int t, int kvh) {
-    const int page = S.page_table[t / S.page_size];
+// pt: the page table, staged in shared memory
+__device__ __forceinline__ size_t kv_off(const PersistState &S, const int *pt, int layer, int t, int kvh) {
+    const int page = pt[t / S.page_size];
     const int slot = t - (t / S.page_size) * S.page_size;
     return (size_t)layer * S.kv_layer_stride + (((size_t)page * NKV + kvh) * S.page_size + slot) * D;
 }
 
-// smem layout (bytes): q16 [I] int16 | xs [I] f32 | ts [I] f32 | sp [2][kSliceMax] f32
-struct PSmem {
-    int16_t *q16;
-    float *xs, *ts, *sp;
-};
-
-}  // namespace
-
-namespace {
-
-template <int IT>
-__device__ __forceinline__ void load_row(const int8_t *__restrict wrow, int lane, uint4 (&w)[IT]) {
-#pragma unroll
-    for (int it = 0; it < IT; ++it) w[it] = ld_stream_v4(wrow + (size_t)(it * 32 + lane) * 16);
+// ---------------------------------------------------------------- weight ring
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
 }
 
-// One output row of an M=1 GEMV with per-row weight scale, in the reference's
-// 8-lane order (cpu_f32a_i8f32sb_f32c_avx2.cpp:181-223), from weights already
-// loaded by load_row.  q_s: the int16 activations in shared memory as int4
-// pairs.  Valid in all lanes.
-template <int IT>
-__device__ __forceinline__ float dot_row(const uint4 (&w)[IT], const int4 *q_s, float a_s, float w_s, int lane) {
-    int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-    for (int it = 0; it < IT; ++it) {
-        const int c = it * 32 + lane;
-        madd_chunk(w[it], q_s[2 * c], q_s[2 * c + 1], p);
+// Position in this CTA's stream: layer, matrix phase, unit index j, stage s.
+struct Cursor {
+    int l, ph, j, s;
+};
+
+// Skip phases in which this CTA owns no unit.
+// cnt[ph]: this CTA's unit count of each matrix phase.
+__device__ __forceinline__ void cursor_settle(Cursor &c, int layers, const int *cnt) {
+    while (c.ph != PH_DONE && cnt[c.ph] == 0) {
+        if (c.ph < PH_DOWN) ++c.ph;
+        else if (c.ph == PH_DOWN) { if (c.l + 1 < layers) { ++c.l; c.ph = PH_QKV; } else c.ph = PH_LM; }
+        else c.ph = PH_DONE;
     }
+}
+__device__ __forceinline__ void cursor_next(Cursor &c, int layers, const int *cnt) {
+    if (++c.s < ph_subs(c.ph)) return;
+    c.s = 0;
+    if (++c.j < cnt[c.ph]) return;
+    c.j = 0;
+    if (c.ph < PH_DOWN) ++c.ph;
+    else if (c.ph == PH_DOWN) { if (c.l + 1 < layers) { ++c.l; c.ph = PH_QKV; } else c.ph = PH_LM; }
+    else c.ph = PH_DONE;
+    cursor_settle(c, layers, cnt);
+}
+
+// Global address of the first row segment of stage (c) and the row stride.
+__device__ __forceinline__ const int8_t *cursor_src(const Cursor &c, const PersistWeights &W, size_t &stride) {
+    const int u = (int)blockIdx.x + c.j * (int)gridDim.x;
+    const size_t l = (size_t)c.l;
+    stride = H;
+    switch (c.ph) {
+    case PH_QKV: {
+        const int r = u * kRows;
+        if (r < NH * D) return W.wq + (l * NH * D + r) * H;
+        if (r < NH * D + NKV * D) return W.wk + (l * NKV * D + (r - NH * D)) * H;
+        return W.wv + (l * NKV * D + (r - NH * D - NKV * D)) * H;
+    }
+    case PH_O: return W.wo + (l * H + (size_t)u * kRows) * H;
+    case PH_GU: return (c.s == 0 ? W.wg : W.wu) + (l * I + (size_t)u * kRows) * H;
+    case PH_DOWN: stride = I; return W.wd + (l * H + (size_t)u * kRows) * I + (size_t)c.s * kSegBytes;
+    default: return W.embed + (size_t)u * kRows * H;
+    }
+}
+
+// Global address of the 16 per-row scales of stage (c) (64 contiguous bytes).
+__device__ __forceinline__ const float *cursor_scales(const Cursor &c, const PersistWeights &W) {
+    const int u = (int)blockIdx.x + c.j * (int)gridDim.x;
+    const size_t l = (size_t)c.l, r = (size_t)u * kRows;
+    switch (c.ph) {
+    case PH_QKV:
+        if (r < (size_t)NH * D) return W.sq + l * NH * D + r;
+        if (r < (size_t)NH * D + NKV * D) return W.sk + l * NKV * D + (r - NH * D);
+        return W.sv + l * NKV * D + (r - NH * D - NKV * D);
+    case PH_O: return W.so + l * H + r;
+    case PH_GU: return (c.s == 0 ? W.sg : W.su) + l * I + r;
+    case PH_DOWN: return W.sd + l * H + r;
+    default: return W.embed_s + r;
+    }
+}
+
+// Ring state, in shared memory: the next stage to issue and its place in
+// the stream.
+struct Producer {
+    Cursor c;
+    int cnt[PH_DONE];   // this CTA's unit count per matrix phase
+    int issued;
+    uint64_t policy;
+};
+
+// Issue the next stage of the stream into its ring slot (whose previous
+// contents every warp has released), if the stream has one left.
+__device__ __forceinline__ void issue_next(Producer &p, const PersistWeights &W, uint32_t ring, uint32_t ring_s,
+                                           uint32_t full_bar) {
+    if (p.c.ph == PH_DONE) return;
+    const int st = p.issued % kStages;
+    size_t stride;
+    const int8_t *src = cursor_src(p.c, W, stride);
+    const uint32_t bar = full_bar + 8 * st;
+    const uint32_t dst = ring + (uint32_t)st * kStageBytes;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic reads of the slot before the copy
+    tc::mbar_expect_tx(bar, kStageBytes + kRows * 4);
+    bulk_g2s(ring_s + (uint32_t)st * kRows * 4, cursor_scales(p.c, W), kRows * 4, bar, p.policy);
+    if (stride == kSegBytes) {
+        bulk_g2s(dst, src, kStageBytes, bar, p.policy);
+    } else {
+#pragma unroll 1
+        for (int r = 0; r < kRows; ++r) bulk_g2s(dst + r * kSegBytes, src + (size_t)r * stride, kSegBytes, bar, p.policy);
+    }
+    ++p.issued;
+    cursor_next(p.c, W.layers, p.cnt);
+}
+
+// This lane's activation chunks [cbase, cbase + 128) of q_s (int16 pairs),
+// held in registers for every row of a phase.
+struct Act {
+    int4 a[8];
+};
+__device__ __forceinline__ void load_act(const int4 *q_s, int cbase, int lane, Act &act) {
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int c = cbase + it * 32 + lane;
+        act.a[2 * it] = q_s[2 * c];
+        act.a[2 * it + 1] = q_s[2 * c + 1];
+    }
+}
+
+// int32 lane sums of one 2048-byte row segment (this warp's row of a stage)
+// against the register-held activation chunks.
+__device__ __forceinline__ void madd_seg(const unsigned char *stage, int warp, int lane, const Act &act, int p[8]) {
+    const uint4 *row = reinterpret_cast<const uint4 *>(stage + warp * kSegBytes);
+    uint4 w[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) w[it] = row[it * 32 + lane];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) madd_chunk(w[it], act.a[2 * it], act.a[2 * it + 1], p);
+}
+
+// Row result from the int32 lane sums, in the reference's 8-lane order
+// (cpu_f32a_i8f32sb_f32c_avx2.cpp:181-223): lane sums reduced over the warp,
+// each lane's sum scaled (one group: the whole row), lanes added pairwise.
+// Valid in all lanes.
+__device__ __forceinline__ float finish_row(int (&p)[8], float a_s, float w_s, int lane) {
     const unsigned full = 0xffffffffu;
     bool up = lane & 16;
 #pragma unroll
@@ -141,74 +303,126 @@ __device__ __forceinline__ float dot_row(const uint4 (&w)[IT], const int4 *q_s, 
     return add_rn(pp, __shfl_xor_sync(full, pp, 8));
 }
 
-// Rows k = 0 .. count-1 of this warp's share of an M=1 GEMV with K = 512*IT,
-// the next row's loads issued before the current row is reduced.
-// row(k, &wrow, &ws) selects the weight row; emit(k, out) consumes the
-// result (valid in all lanes).
-template <int IT, typename RowFn, typename EmitFn>
-__device__ __forceinline__ void gemv_rows(int count, const int4 *q_s, float a_s, int lane, RowFn row, EmitFn emit) {
-    if (count <= 0) return;
-    if constexpr (IT > 4) {            // long rows: no second register set
-        for (int k = 0; k < count; ++k) {
-            uint4 w[IT];
-            const int8_t *wr;
-            float ws;
-            row(k, wr, ws);
-            load_row<IT>(wr, lane, w);
-            emit(k, dot_row<IT>(w, q_s, a_s, ws, lane));
-        }
-        return;
-    }
-    uint4 w[IT], nx[IT];
-    const int8_t *wr;
-    float ws, nws = 0.0f;
-    row(0, wr, ws);
-    load_row<IT>(wr, lane, w);
-    for (int k = 0; k < count; ++k) {
-        if (k + 1 < count) {
-            const int8_t *nwr;
-            row(k + 1, nwr, nws);
-            load_row<IT>(nwr, lane, nx);
-        }
-        emit(k, dot_row<IT>(w, q_s, a_s, ws, lane));
-#pragma unroll
-        for (int i = 0; i < IT; ++i) w[i] = nx[i];
-        ws = nws;
-    }
-}
-
-// Rows first, first + stride, ... below n_rows.
-__device__ __forceinline__ int strided_count(int first, int stride, int n_rows) {
-    return first < n_rows ? (n_rows - first + stride - 1) / stride : 0;
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kPThreads, 1)
 decode_persistent_kernel(PersistWeights W, PersistState S) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    int16_t *q16 = reinterpret_cast<int16_t *>(smraw);
-    float *xs = reinterpret_cast<float *>(smraw + (size_t)I * sizeof(int16_t));
+    extern __shared__ __align__(1024) unsigned char smraw[];
+    unsigned char *ring_ptr = smraw;
+    int16_t *q16 = reinterpret_cast<int16_t *>(smraw + kRingBytes);
+    float *xs = reinterpret_cast<float *>(smraw + kRingBytes + (size_t)I * sizeof(int16_t));
     float *ts = xs + I;
-    float *sp = ts + I;
+    float *sp = ts + H;
     const int4 *q_s = reinterpret_cast<const int4 *>(q16);
+    float *nrm_w = sp + 2 * kSliceMax;     // [H] next RMSNorm weight (dequantised int8 value)
+    float *nrm_s = nrm_w + H;               // [H / norm_group] its group scales
+    __shared__ __align__(8) uint64_t full_mb[kStages];
+    __shared__ __align__(16) float ring_scales[kStages][kRows];   // per-row weight scales of each stage
+    __shared__ int released[kStages];
+    __shared__ Producer prod;
     __shared__ float scratch[65];
     __shared__ float a_s_sh;
-    __shared__ unsigned gen0;
+    __shared__ int aborted_at_entry;
+    __shared__ int pt_sm[kMaxPages];
     __shared__ float head_m[NH], head_inv[NH];
     __shared__ float redf[2][kPWarps];
     __shared__ double redd[2][kPWarps];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = blockIdx.x * kPWarps + warp, nw = gridDim.x * kPWarps;
     const int ng = W.norm_group;
     const float eps = W.eps;
-    if (threadIdx.x == 0) gen0 = ld_volatile(S.bar_gen);
+    const uint32_t ring = tc::smem_u32(ring_ptr);
+    const uint32_t full_bar = tc::smem_u32(full_mb);
+    const uint32_t ring_s = tc::smem_u32(&ring_scales[0][0]);
+    int cons = 0;                       // stages consumed (same count in every thread)
+    int nsync = 0;                      // grid barriers passed
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) S.trace[0] = global_ns();
+        // a workspace left aborted by an earlier call: decode nothing
+        aborted_at_entry = ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag)) != 0;
+        for (int i = 0; i < kStages; ++i) {
+            tc::mbar_init(full_bar + 8 * i, 1);
+            released[i] = 0;
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prod.c = Cursor{0, PH_QKV, 0, 0};
+        prod.issued = 0;
+        prod.policy = evict_first_policy();
+        for (int ph = 0; ph < PH_DONE; ++ph) prod.cnt[ph] = cta_units(ph_units(ph, W.vocab));
+        cursor_settle(prod.c, W.layers, prod.cnt);
+        if (!aborted_at_entry)
+            for (int i = 0; i < kStages; ++i) issue_next(prod, W, ring, ring_s, full_bar);
+    }
+    for (int i = threadIdx.x; i < (S.max_ctx + S.page_size - 1) / S.page_size; i += kPThreads)
+        pt_sm[i] = S.page_table[i];
     __syncthreads();
-    unsigned gen = gen0;
+    if (aborted_at_entry) return;
     const int token = S.token[0];
     const int pos = S.pos[0];
     const int ctx = min(pos + 1, S.max_ctx);
+
+    // Wait (bounded) for every stage still in flight, so that no copy
+    // targets shared memory after the CTA has left.
+    auto drain = [&]() {
+        if (threadIdx.x == 0)
+            for (int k = max(0, prod.issued - kStages); k < prod.issued; ++k)
+                tc::mbar_wait(full_bar + 8 * (k % kStages), (k / kStages) & 1, nullptr);
+    };
+#ifdef QVL_PERSIST_DETAIL
+#define DETAIL(slot) do { if (blockIdx.x == 0 && threadIdx.x == 0) S.trace[slot] = global_ns(); } while (0)
+#else
+#define DETAIL(slot) do { } while (0)
+#endif
+#define SYNC_OR_EXIT()                                                                    \
+    do {                                                                                  \
+        if (!grid_sync(S, nsync)) { drain(); return; }                                    \
+    } while (0)
+
+    // Run fn(stage) on the next stage of the ring once it has landed (all
+    // lanes), then release it; the last warp to release a slot refills it
+    // with the stream's next stage (stages are released, and so issued, in
+    // order: a warp issues before it moves on to the next stage).
+    auto consume = [&](auto &&fn) {
+        const int st = cons % kStages;
+        bool ok = tc::mbar_wait(full_bar + 8 * st, (cons / kStages) & 1, S.abort_flag);
+        ok = __any_sync(0xffffffffu, ok);          // the phase completes once for all lanes
+        if (ok) fn(ring_ptr + (size_t)st * kStageBytes, ring_scales[st][warp]);
+        __syncwarp();
+        // (the slot's values are already consumed by the arithmetic above,
+        // so no fence: a fence here would also wait for this lane's global
+        // stores to complete)
+        if (lane == 0 && atomicAdd(&released[st], 1) == kPWarps - 1) {
+            released[st] = 0;
+            issue_next(prod, W, ring, ring_s, full_bar);
+        }
+        ++cons;
+        __syncwarp();
+    };
+
+    // Stage RMSNorm weights (int8 -> float, group scales) in shared memory;
+    // done before the barrier that precedes the norm.  Reads them after
+    // the CTA barrier at the top of the next grid barrier.
+    auto stage_norm = [&](const int8_t *wq, const float *wsc) {
+        for (int j = threadIdx.x; j < H; j += kPThreads) nrm_w[j] = (float)__ldg(wq + j);
+        for (int j = threadIdx.x; j < H / ng; j += kPThreads) nrm_s[j] = __ldg(wsc + j);
+    };
+    // x (residual, written by other CTAs) -> RMSNorm with the staged weight
+    // -> quantisation (one scale) into q16 / a_s_sh; arithmetic of
+    // cta_norm_quant_row.
+    auto norm_quant_x = [&](bool inplace_form) {
+        for (int i = threadIdx.x; i < H / 4; i += kPThreads)
+            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.x) + i);
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const float ss = rms_sumsq_ref(xs, H);
+            if (threadIdx.x == 0) scratch[64] = rms_inv(ss, H, eps, inplace_form);
+        }
+        __syncthreads();
+        const float inv = scratch[64];
+        for (int j = threadIdx.x; j < H; j += kPThreads) ts[j] = mul_rn(nrm_w[j], mul_rn(mul_rn(nrm_s[j / ng], inv), xs[j]));
+        __syncthreads();
+        cta_quantize_smem_row(ts, H, H, q16, &a_s_sh, scratch);
+    };
 
     // embedding_lookup (per-row scale) of the input token into the residual stream
     if (blockIdx.x == 0) {
@@ -216,31 +430,60 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         const float sc = W.embed_s[id];
         for (int j = threadIdx.x; j < H; j += kPThreads) S.x[j] = mul_rn((float)W.embed[(size_t)id * H + j], sc);
     }
-    if (!grid_sync(S, gen)) return;
+    stage_norm(W.in_norm, W.in_norm_s);
+    SYNC_OR_EXIT();
+
+    const int per = (ctx + kSlices - 1) / kSlices;
+    const bool attn_cta = blockIdx.x < NKV * kSlices;
+    const int kvh = blockIdx.x / kSlices, sl = blockIdx.x % kSlices;
+    const int t0 = min(ctx, sl * per), t1 = min(ctx, t0 + per), len = t1 - t0;
+    const int t16 = threadIdx.x & 15, hw = threadIdx.x >> 4;
 
     for (int l = 0; l < W.layers; ++l) {
-        // ---- input rms_norm + quantisation (every CTA), q/k/v rows over all warps
-        cta_norm_quant_row(S.x, W.in_norm + (size_t)l * H, W.in_norm_s + (size_t)l * (H / ng), ng, eps, false,
-                           nullptr, q16, &a_s_sh, H, H, xs, ts, scratch);
-        gemv_rows<4>(strided_count(gw, nw, NH * D + 2 * NKV * D), q_s, a_s_sh, lane,
-            [&](int k, const int8_t *&wr, float &ws) {
-                const int n = gw + k * nw;
-                if (n < NH * D) {
-                    wr = W.wq + ((size_t)l * NH * D + n) * H; ws = __ldg(W.sq + (size_t)l * NH * D + n);
-                } else if (n < NH * D + NKV * D) {
-                    const int r = n - NH * D;
-                    wr = W.wk + ((size_t)l * NKV * D + r) * H; ws = __ldg(W.sk + (size_t)l * NKV * D + r);
-                } else {
-                    const int r = n - NH * D - NKV * D;
-                    wr = W.wv + ((size_t)l * NKV * D + r) * H; ws = __ldg(W.sv + (size_t)l * NKV * D + r);
-                }
-            },
-            [&](int k, float out) { if (lane == 0) S.qkv[gw + k * nw] = out; });
-        if (!grid_sync(S, gen)) return;
+        // this layer's cached K/V rows of the slice (all but the new token) into L2
+        if (attn_cta) {
+            const int n_old = min(len, max(0, pos - t0));
+            for (int e = threadIdx.x; e < 4 * n_old; e += kPThreads) {
+                const int t = e >> 2, half = e & 1;
+                const uint16_t *base = (e & 2) ? S.v_pages : S.k_pages;
+                prefetch_l2(base + kv_off(S, pt_sm, l, t0 + t, kvh) + half * (D / 2));
+            }
+        }
+        // ---- input rms_norm + quantisation (every CTA), q/k/v blocks of the ring
+        norm_quant_x(false);
+        if (l == 5) DETAIL(230);
+        {
+            const int nu = cta_units(ph_units(PH_QKV, W.vocab));
+            Act act;
+            load_act(q_s, 0, lane, act);
+            for (int j = 0; j < nu; ++j) {
+                const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
+                consume([&](const unsigned char *st, float sc) {
+                    int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    madd_seg(st, warp, lane, act, p);
+                    const float out = finish_row(p, a_s_sh, sc, lane);
+                    if (lane == 0) S.qkv[n] = out;
+                });
+            }
+        }
+        if (l == 5) DETAIL(231);
+        // this CTA's QK-norm weight and RoPE row, read before the barrier
+        const bool qk_cta = blockIdx.x < NH + (pos < S.max_ctx ? NKV : 0);
+        float qk_w = 0.0f, qk_s = 0.0f, rc = 0.0f, rs = 0.0f;
+        if (qk_cta && threadIdx.x < D) {
+            const bool isq = blockIdx.x < NH;
+            qk_w = (float)__ldg((isq ? W.q_norm : W.k_norm) + (size_t)l * D + threadIdx.x);
+            qk_s = __ldg((isq ? W.q_norm_s : W.k_norm_s) + (size_t)l * (D / ng) + threadIdx.x / ng);
+            if (threadIdx.x < D / 2) {
+                rc = __ldg(S.rope_cos + (size_t)pos * (D / 2) + threadIdx.x);
+                rs = __ldg(S.rope_sin + (size_t)pos * (D / 2) + threadIdx.x);
+            }
+        }
+        SYNC_OR_EXIT();
 
         // ---- QK rms_norm_inplace + RoPE (q written back; k, v appended as fp16)
         // (a position past the cache is not appended; the host keeps pos < max_ctx)
-        if (blockIdx.x < NH + (pos < S.max_ctx ? NKV : 0)) {
+        if (qk_cta) {
             const bool isq = blockIdx.x < NH;
             const int hh = isq ? blockIdx.x : blockIdx.x - NH;
             const float *src = S.qkv + (isq ? hh * D : NH * D + hh * D);
@@ -251,42 +494,31 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 if (threadIdx.x == 0) scratch[64] = rms_inv(ss, D, eps, true);
             }
             __syncthreads();
-            const int8_t *nwq = (isq ? W.q_norm : W.k_norm) + (size_t)l * D;
-            const float *nws = (isq ? W.q_norm_s : W.k_norm_s) + (size_t)l * (D / ng);
-            if (threadIdx.x < D)
-                ts[threadIdx.x] = mul_rn((float)nwq[threadIdx.x],
-                                         mul_rn(mul_rn(nws[threadIdx.x / ng], scratch[64]), xs[threadIdx.x]));
+            if (threadIdx.x < D) ts[threadIdx.x] = mul_rn(qk_w, mul_rn(mul_rn(qk_s, scratch[64]), xs[threadIdx.x]));
             __syncthreads();
-            const float *c = S.rope_cos + (size_t)pos * (D / 2);
-            const float *s = S.rope_sin + (size_t)pos * (D / 2);
             if (threadIdx.x < D / 2) {
                 const int j = threadIdx.x;
                 const float x1 = ts[j], x2 = ts[j + D / 2];
-                const float y1 = fma_rn(x1, c[j], -mul_rn(x2, s[j]));
-                const float y2 = fma_rn(x1, s[j], mul_rn(x2, c[j]));
+                const float y1 = fma_rn(x1, rc, -mul_rn(x2, rs));
+                const float y2 = fma_rn(x1, rs, mul_rn(x2, rc));
                 if (isq) {
                     S.qkv[hh * D + j] = y1;
                     S.qkv[hh * D + j + D / 2] = y2;
                 } else {
-                    const size_t off = kv_off(S, l, pos, hh);
+                    const size_t off = kv_off(S, pt_sm, l, pos, hh);
                     S.k_pages[off + j] = __half_as_ushort(__float2half_rn(y1));
                     S.k_pages[off + j + D / 2] = __half_as_ushort(__float2half_rn(y2));
                 }
             }
             if (!isq && threadIdx.x < D) {
-                const size_t off = kv_off(S, l, pos, hh);
+                const size_t off = kv_off(S, pt_sm, l, pos, hh);
                 S.v_pages[off + threadIdx.x] =
                     __half_as_ushort(__float2half_rn(__ldcg(S.qkv + NH * D + NKV * D + hh * D + threadIdx.x)));
             }
         }
-        if (!grid_sync(S, gen)) return;
+        SYNC_OR_EXIT();
 
         // ---- attention, phase 1: scores of one context slice and its maximum
-        const int per = (ctx + kSlices - 1) / kSlices;
-        const bool attn_cta = blockIdx.x < NKV * kSlices;
-        const int kvh = blockIdx.x / kSlices, sl = blockIdx.x % kSlices;
-        const int t0 = min(ctx, sl * per), t1 = min(ctx, t0 + per), len = t1 - t0;
-        const int t16 = threadIdx.x & 15, hw = threadIdx.x >> 4;
         if (attn_cta) {
             float qv[2][8];
 #pragma unroll
@@ -301,7 +533,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int t = tb + 32 * u;
-                    kr[u] = (t < len) ? __ldcg(reinterpret_cast<const uint4 *>(S.k_pages + kv_off(S, l, t0 + t, kvh)) + t16)
+                    kr[u] = (t < len) ? __ldcg(reinterpret_cast<const uint4 *>(S.k_pages + kv_off(S, pt_sm, l, t0 + t, kvh)) + t16)
                                       : make_uint4(0, 0, 0, 0);
                 }
 #pragma unroll
@@ -338,7 +570,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 S.att_lmax[(kvh * 2 + threadIdx.x) * kSlices + sl] = m;
             }
         }
-        if (!grid_sync(S, gen)) return;
+        SYNC_OR_EXIT();
 
         // ---- attention, phase 2: probabilities (global max), slice sum, partial P.V
         if (attn_cta) {
@@ -378,7 +610,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int t = tb + 32 * u;
-                    vr[u] = (t < len) ? __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, l, t0 + t, kvh)) + t16)
+                    vr[u] = (t < len) ? __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, pt_sm, l, t0 + t, kvh)) + t16)
                                       : make_uint4(0, 0, 0, 0);
                 }
 #pragma unroll
@@ -409,7 +641,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 S.att_pacc[((kvh * 2 + h) * kSlices + sl) * D + dd] = s2;
             }
         }
-        if (!grid_sync(S, gen)) return;
+        SYNC_OR_EXIT();
 
         // ---- attention combine (every CTA) -> quantisation -> o_proj + residual
         if (threadIdx.x < NH) {
@@ -435,76 +667,125 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         }
         __syncthreads();
         cta_quantize_smem_row(xs, H, H, q16, &a_s_sh, scratch);
-        gemv_rows<4>(strided_count(gw, nw, H), q_s, a_s_sh, lane,
-            [&](int k, const int8_t *&wr, float &ws) {
-                const int n = gw + k * nw;
-                wr = W.wo + ((size_t)l * H + n) * H; ws = __ldg(W.so + (size_t)l * H + n);
-            },
-            [&](int k, float out) {
-                const int n = gw + k * nw;
-                if (lane == 0) S.x[n] = add_rn(__ldcg(S.x + n), out);
-            });
-        if (!grid_sync(S, gen)) return;
+        {
+            const int nu = cta_units(ph_units(PH_O, W.vocab));
+            Act act;
+            load_act(q_s, 0, lane, act);
+            for (int j = 0; j < nu; ++j) {
+                const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
+                const float xn = lane == 0 ? __ldcg(S.x + n) : 0.0f;
+                consume([&](const unsigned char *st, float sc) {
+                    int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    madd_seg(st, warp, lane, act, p);
+                    const float out = finish_row(p, a_s_sh, sc, lane);
+                    if (lane == 0) S.x[n] = add_rn(xn, out);
+                });
+            }
+        }
+        stage_norm(W.post_norm + (size_t)l * H, W.post_norm_s + (size_t)l * (H / ng));
+        SYNC_OR_EXIT();
 
         // ---- post-attention rms_norm + quantisation (every CTA), gate/up + SwiGLU
-        cta_norm_quant_row(S.x, W.post_norm + (size_t)l * H, W.post_norm_s + (size_t)l * (H / ng), ng, eps, false,
-                           nullptr, q16, &a_s_sh, H, H, xs, ts, scratch);
+        norm_quant_x(false);
+        if (l == 5) DETAIL(232);
+
         {
-            float gate_v = 0.0f;
-            // the warp's k-th row: gate (k even) or up (k odd) row p = gw + (k/2)*nw
-            gemv_rows<4>(2 * strided_count(gw, nw, I), q_s, a_s_sh, lane,
-                [&](int k, const int8_t *&wr, float &ws) {
-                    const int p = gw + (k >> 1) * nw;
-                    if ((k & 1) == 0) { wr = W.wg + ((size_t)l * I + p) * H; ws = __ldg(W.sg + (size_t)l * I + p); }
-                    else { wr = W.wu + ((size_t)l * I + p) * H; ws = __ldg(W.su + (size_t)l * I + p); }
-                },
-                [&](int k, float out) {
-                    if ((k & 1) == 0) gate_v = out;
-                    else if (lane == 0) S.h[gw + (k >> 1) * nw] = swiglu_one(gate_v, out);
+            const int nu = cta_units(ph_units(PH_GU, W.vocab));
+            Act act;
+            load_act(q_s, 0, lane, act);
+            for (int j = 0; j < nu; ++j) {
+                const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
+                float gate_v = 0.0f;
+#ifdef QVL_PERSIST_DETAIL
+                if (l == 5 && j == 0 && threadIdx.x == 0) {
+                    const int st0 = cons % kStages;
+                    S.trace[512 + blockIdx.x] = tc::mbar_try_wait(full_bar + 8 * st0, (cons / kStages) & 1) ? 1 : 0;
+                }
+#endif
+                consume([&](const unsigned char *st, float sc) {
+                    int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    madd_seg(st, warp, lane, act, p);
+                    gate_v = finish_row(p, a_s_sh, sc, lane);
                 });
+#ifdef QVL_PERSIST_DETAIL
+                if (l == 5 && j == 0 && threadIdx.x == 0) S.trace[822 + blockIdx.x] = global_ns();
+#endif
+                consume([&](const unsigned char *st, float sc) {
+                    int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    madd_seg(st, warp, lane, act, p);
+                    const float up = finish_row(p, a_s_sh, sc, lane);
+                    if (lane == 0) S.h[n] = swiglu_one(gate_v, up);
+                });
+                if (l == 5) DETAIL(234 + j);
+#ifdef QVL_PERSIST_DETAIL
+                if (l == 5 && threadIdx.x == 0 && j < 2) { if (j == 0) S.trace[672 + blockIdx.x] = global_ns(); }
+#endif
+            }
         }
-        if (!grid_sync(S, gen)) return;
+        if (l == 5) DETAIL(233);
+#ifdef QVL_PERSIST_DETAIL
+        if (l == 5 && threadIdx.x == 0) S.trace[256 + blockIdx.x] = global_ns();
+#endif
+        SYNC_OR_EXIT();
 
         // ---- quantisation of the SwiGLU row (every CTA), down + residual
         for (int i = threadIdx.x; i < I / 4; i += kPThreads)
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.h) + i);
         __syncthreads();
         cta_quantize_smem_row(xs, I, I, q16, &a_s_sh, scratch);
-        gemv_rows<12>(strided_count(gw, nw, H), q_s, a_s_sh, lane,
-            [&](int k, const int8_t *&wr, float &ws) {
-                const int n = gw + k * nw;
-                wr = W.wd + ((size_t)l * H + n) * I; ws = __ldg(W.sd + (size_t)l * H + n);
-            },
-            [&](int k, float out) {
-                const int n = gw + k * nw;
-                if (lane == 0) S.x[n] = add_rn(__ldcg(S.x + n), out);
-            });
-        if (!grid_sync(S, gen)) return;
+        {
+            const int nu = cta_units(ph_units(PH_DOWN, W.vocab));
+            for (int j = 0; j < nu; ++j) {
+                const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
+                float ws = 0.0f;
+                const float xn = lane == 0 ? __ldcg(S.x + n) : 0.0f;
+                int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int s = 0; s < I / kSegBytes; ++s)
+                    consume([&](const unsigned char *st, float sc) {
+                        Act act;
+                        load_act(q_s, s * (kSegBytes / 16), lane, act);
+                        madd_seg(st, warp, lane, act, p);
+                        ws = sc;
+                    });
+                const float out = finish_row(p, a_s_sh, ws, lane);
+                if (lane == 0) S.x[n] = add_rn(xn, out);
+            }
+        }
+        if (l + 1 < W.layers) stage_norm(W.in_norm + (size_t)(l + 1) * H, W.in_norm_s + (size_t)(l + 1) * (H / ng));
+        else stage_norm(W.final_norm, W.final_norm_s);
+        SYNC_OR_EXIT();
     }
 
     // ---- final rms_norm_inplace + quantisation (every CTA), LM head + greedy
-    cta_norm_quant_row(S.x, W.final_norm, W.final_norm_s, ng, eps, true, nullptr, q16, &a_s_sh, H, H, xs, ts,
-                       scratch);
+    norm_quant_x(true);
     {
         float best_v = -FLT_MAX;
         int best_i = INT_MAX;
-        gemv_rows<4>(strided_count(gw, nw, W.vocab), q_s, a_s_sh, lane,
-            [&](int k, const int8_t *&wr, float &ws) {
-                const int n = gw + k * nw;
-                wr = W.embed + (size_t)n * H; ws = __ldg(W.embed_s + n);
-            },
-            [&](int k, float out) {
-                const int n = gw + k * nw;
+        const int nu = cta_units(ph_units(PH_LM, W.vocab));
+        Act act;
+        load_act(q_s, 0, lane, act);
+        DETAIL(200);
+        for (int j = 0; j < nu; ++j) {
+            if ((j & 7) == 7) DETAIL(201 + (j >> 3));
+            const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
+            consume([&](const unsigned char *st, float sc) {
+                int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                madd_seg(st, warp, lane, act, p);
+                const float out = finish_row(p, a_s_sh, sc, lane);
                 if (lane == 0) S.logits[n] = out;
                 if (out > best_v) { best_v = out; best_i = n; }   // ascending n: strict > keeps the first
             });
+        }
         if (lane == 0) {
+            const int gw = blockIdx.x * kPWarps + warp;
             S.warp_best_v[gw] = best_v;
             S.warp_best_i[gw] = best_i;
         }
     }
-    if (!grid_sync(S, gen)) return;
+    SYNC_OR_EXIT();
+#undef SYNC_OR_EXIT
     if (blockIdx.x == 0) {
+        const int nw = gridDim.x * kPWarps;
         float v = -FLT_MAX;
         int bi = INT_MAX;
         for (int w = threadIdx.x; w < nw; w += kPThreads) {
@@ -534,9 +815,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     }
 }
 
-size_t persist_smem_bytes() {
-    return (size_t)I * sizeof(int16_t) + 2 * (size_t)I * sizeof(float) + 2 * (size_t)kSliceMax * sizeof(float);
-}
+size_t persist_smem_bytes() { return kSmemBytes; }
 
 int persist_grid_ctas() {
     static int cached[64] = {};                 // per device, computed on first use

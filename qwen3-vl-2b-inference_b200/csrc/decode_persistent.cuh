@@ -37,8 +37,9 @@ struct PersistState {
     int page_size;
     const float *rope_cos, *rope_sin;   // [max_pos, D/2]
     int max_ctx;
-    unsigned *bar_count, *bar_gen;      // grid barrier (bar_count 0 between launches)
+    unsigned long long *bar_count;      // grid barrier: arrivals since the workspace was zeroed
     int *abort_flag;                    // set to 1 if a barrier wait timed out
+    unsigned long long *trace;          // [kPersistTraceSlots] kernel start + barrier opening times (ns)
 };
 
 // Dimensions the kernel is compiled for (Qwen3-VL-2B text decoder).
@@ -48,6 +49,7 @@ bool persist_supported(int hidden, int intermediate, int heads, int kv_heads, in
 int persist_grid_ctas();
 constexpr int kPersistWarpsPerCta = 16;
 constexpr int kPersistSlices = 16;
+constexpr unsigned kPersistTraceSlots = 1024;
 cudaError_t launch_decode_persistent(const PersistWeights &w, const PersistState &s, int ctas, cudaStream_t stream);
 
 }  // namespace qvl
