@@ -41,8 +41,9 @@
 namespace qvl {
 
 namespace {
-constexpr int kPThreads = 512;
+constexpr int kPThreads = 512;                 // compute threads (16 warps)
 constexpr int kPWarps = kPThreads / 32;
+constexpr int kBlock = kPThreads + 32;         // + one producer warp that feeds the weight ring
 constexpr int H = 2048, I = 6144, NH = 16, NKV = 8, D = 128;
 constexpr int kSlices = kPersistSlices;        // attention context slices per KV head
 constexpr int kSliceMax = 512;                 // tokens per slice (context <= 8192)
@@ -80,6 +81,10 @@ __device__ __forceinline__ int cta_units(int U) {
 __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
     return *reinterpret_cast<const volatile unsigned *>(p);
 }
+// Barrier of the 16 compute warps only (named barrier 1); the producer warp
+// never joins it.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kPThreads) : "memory"); }
+
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -94,7 +99,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // release).  Returns false if the wait gave up or another CTA aborted.
 // CTA 0 records the time each barrier opens in S.trace[1 + k].
 __device__ __forceinline__ bool grid_sync(const PersistState &S, int &nsync) {
-    __syncthreads();
+    csync();
     __shared__ int ok;
     if (threadIdx.x == 0) {
         unsigned long long old, v;
@@ -121,7 +126,7 @@ __device__ __forceinline__ bool grid_sync(const PersistState &S, int &nsync) {
         if (blockIdx.x == 0 && (unsigned)nsync + 1 < kTraceSlots) S.trace[nsync + 1] = global_ns();
     }
     ++nsync;
-    __syncthreads();
+    csync();
     return ok;
 }
 
@@ -228,24 +233,84 @@ struct Producer {
 // Issue the next stage of the stream into its ring slot (whose previous
 // contents every warp has released), if the stream has one left.
 __device__ __forceinline__ void issue_next(Producer &p, const PersistWeights &W, uint32_t ring, uint32_t ring_s,
-                                           uint32_t full_bar) {
+                                           uint32_t full_bar, unsigned long long *dbg = nullptr) {
     if (p.c.ph == PH_DONE) return;
     const int st = p.issued % kStages;
     size_t stride;
     const int8_t *src = cursor_src(p.c, W, stride);
+    const float *ssrc = cursor_scales(p.c, W);
     const uint32_t bar = full_bar + 8 * st;
     const uint32_t dst = ring + (uint32_t)st * kStageBytes;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic reads of the slot before the copy
+    if (dbg) dbg[0] = global_ns();
     tc::mbar_expect_tx(bar, kStageBytes + kRows * 4);
-    bulk_g2s(ring_s + (uint32_t)st * kRows * 4, cursor_scales(p.c, W), kRows * 4, bar, p.policy);
+    bulk_g2s(ring_s + (uint32_t)st * kRows * 4, ssrc, kRows * 4, bar, p.policy);
+    if (dbg) dbg[1] = global_ns();
     if (stride == kSegBytes) {
         bulk_g2s(dst, src, kStageBytes, bar, p.policy);
     } else {
 #pragma unroll 1
         for (int r = 0; r < kRows; ++r) bulk_g2s(dst + r * kSegBytes, src + (size_t)r * stride, kSegBytes, bar, p.policy);
     }
+    if (dbg) dbg[2] = global_ns();
     ++p.issued;
     cursor_next(p.c, W.layers, p.cnt);
+}
+
+// The producer lane: streams every stage of this CTA in order, each into
+// its slot once all compute warps have released the slot's previous stage.
+// Leaves at the end of the stream, when the compute warps set *stop, or
+// after a bounded wait (abort flag set); then sets *done.
+__device__ __noinline__ void produce(Producer &p, const PersistWeights &W, uint32_t ring, uint32_t ring_s,
+                                     uint32_t full_bar, uint32_t empty_bar, int *abort_flag, int *stop,
+                                     int *issued_out, int *done) {
+    volatile int *vstop = stop;
+    p.c = Cursor{0, PH_QKV, 0, 0};
+    p.issued = 0;
+    p.policy = evict_first_policy();
+    for (int ph = 0; ph < PH_DONE; ++ph) p.cnt[ph] = cta_units(ph_units(ph, W.vocab));
+    cursor_settle(p.c, W.layers, p.cnt);
+    while (p.c.ph != PH_DONE && *vstop == 0) {
+        const int k = p.issued, st = k % kStages;
+        if (k >= kStages) {
+            const uint32_t bar = empty_bar + 8 * st, parity = ((k / kStages) - 1) & 1;
+            const unsigned long long t0 = global_ns();
+            bool ok = true;
+            while (!tc::mbar_try_wait(bar, parity)) {
+                if (*vstop) { ok = false; break; }
+                if (global_ns() - t0 > kBarrierLimitNs) {
+                    atomicExch(abort_flag, 1);
+                    ok = false;
+                    break;
+                }
+            }
+            if (!ok) break;
+        }
+        issue_next(p, W, ring, ring_s, full_bar);
+        *reinterpret_cast<volatile int *>(issued_out) = p.issued;
+    }
+    __threadfence_block();
+    *reinterpret_cast<volatile int *>(done) = 1;
+}
+
+// cta_quantize_smem_row for the compute warps (named barrier, kPThreads):
+// group scales of ts[0..n) (group g, n / g <= 64) and quantisation into q.
+__device__ __forceinline__ void quantize_row_smem(const float *ts, int n, int g, int16_t *q, float *qs,
+                                                  float *scratch) {
+    const int G = n / g;
+    const int hw = threadIdx.x >> 4, nhw = kPThreads >> 4, t16 = threadIdx.x & 15;
+    for (int e0 = hw & ~1; e0 < G; e0 += nhw) {   // both half-warps of a warp take the same trip count
+        const int e_raw = e0 + (hw & 1);
+        const bool active = e_raw < G;
+        const int e = active ? e_raw : e0;
+        const float sc = group_scale_ref(ts + (size_t)e * g, g, t16);
+        if (active && t16 == 0) {
+            qs[e] = sc;
+            scratch[e] = __fdiv_rn(1.0f, sc);
+        }
+    }
+    csync();
+    for (int j = threadIdx.x; j < n; j += kPThreads) q[j] = quant_one(ts[j], scratch[j / g]);
+    csync();
 }
 
 // This lane's activation chunks [cbase, cbase + 128) of q_s (int16 pairs),
@@ -305,7 +370,7 @@ __device__ __forceinline__ float finish_row(int (&p)[8], float a_s, float w_s, i
 
 }  // namespace
 
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(kBlock, 1)
 decode_persistent_kernel(PersistWeights W, PersistState S) {
     extern __shared__ __align__(1024) unsigned char smraw[];
     unsigned char *ring_ptr = smraw;
@@ -318,8 +383,10 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     float *nrm_s = nrm_w + H;               // [H / norm_group] its group scales
     __shared__ __align__(8) uint64_t full_mb[kStages];
     __shared__ __align__(16) float ring_scales[kStages][kRows];   // per-row weight scales of each stage
-    __shared__ int released[kStages];
-    __shared__ Producer prod;
+    __shared__ __align__(8) uint64_t empty_mb[kStages];
+    __shared__ int stop_flag;                  // compute warps leaving early: producer stops
+    __shared__ int issued_sh;                  // stages issued so far (producer -> drain)
+    __shared__ int prod_done;                  // the producer has left
     __shared__ float scratch[65];
     __shared__ float a_s_sh;
     __shared__ int aborted_at_entry;
@@ -332,9 +399,10 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     const int ng = W.norm_group;
     const float eps = W.eps;
     const uint32_t ring = tc::smem_u32(ring_ptr);
-    const uint32_t full_bar = tc::smem_u32(full_mb);
+    const uint32_t full_bar = tc::smem_u32(full_mb), empty_bar = tc::smem_u32(empty_mb);
     const uint32_t ring_s = tc::smem_u32(&ring_scales[0][0]);
-    int cons = 0;                       // stages consumed (same count in every thread)
+    Producer prod;                      // used by the producer lane only
+    int cons = 0;                       // stages consumed (same count in every compute thread)
     int nsync = 0;                      // grid barriers passed
     if (threadIdx.x == 0) {
         if (blockIdx.x == 0) S.trace[0] = global_ns();
@@ -342,21 +410,21 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         aborted_at_entry = ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag)) != 0;
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(full_bar + 8 * i, 1);
-            released[i] = 0;
+            tc::mbar_init(empty_bar + 8 * i, kPWarps);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        prod.c = Cursor{0, PH_QKV, 0, 0};
-        prod.issued = 0;
-        prod.policy = evict_first_policy();
-        for (int ph = 0; ph < PH_DONE; ++ph) prod.cnt[ph] = cta_units(ph_units(ph, W.vocab));
-        cursor_settle(prod.c, W.layers, prod.cnt);
-        if (!aborted_at_entry)
-            for (int i = 0; i < kStages; ++i) issue_next(prod, W, ring, ring_s, full_bar);
+        stop_flag = 0;
+        issued_sh = 0;
+        prod_done = 0;
     }
-    for (int i = threadIdx.x; i < (S.max_ctx + S.page_size - 1) / S.page_size; i += kPThreads)
+    for (int i = threadIdx.x; i < (S.max_ctx + S.page_size - 1) / S.page_size; i += kBlock)
         pt_sm[i] = S.page_table[i];
     __syncthreads();
     if (aborted_at_entry) return;
+    if (warp == kPWarps) {                   // the producer warp
+        if (lane == 0) produce(prod, W, ring, ring_s, full_bar, empty_bar, S.abort_flag, &stop_flag, &issued_sh, &prod_done);
+        return;
+    }
     const int token = S.token[0];
     const int pos = S.pos[0];
     const int ctx = min(pos + 1, S.max_ctx);
@@ -364,9 +432,16 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     // Wait (bounded) for every stage still in flight, so that no copy
     // targets shared memory after the CTA has left.
     auto drain = [&]() {
-        if (threadIdx.x == 0)
-            for (int k = max(0, prod.issued - kStages); k < prod.issued; ++k)
+        if (threadIdx.x == 0) {
+            *reinterpret_cast<volatile int *>(&stop_flag) = 1;
+            // the producer leaves within one issue; then its count is final
+            const unsigned long long t0 = global_ns();
+            while (*reinterpret_cast<volatile int *>(&prod_done) == 0 && global_ns() - t0 < kBarrierLimitNs) {
+            }
+            const int issued = *reinterpret_cast<volatile int *>(&issued_sh);
+            for (int k = max(0, issued - kStages); k < issued; ++k)
                 tc::mbar_wait(full_bar + 8 * (k % kStages), (k / kStages) & 1, nullptr);
+        }
     };
 #ifdef QVL_PERSIST_DETAIL
 #define DETAIL(slot) do { if (blockIdx.x == 0 && threadIdx.x == 0) S.trace[slot] = global_ns(); } while (0)
@@ -378,25 +453,27 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         if (!grid_sync(S, nsync)) { drain(); return; }                                    \
     } while (0)
 
-    // Run fn(stage) on the next stage of the ring once it has landed (all
-    // lanes), then release it; the last warp to release a slot refills it
-    // with the stream's next stage (stages are released, and so issued, in
-    // order: a warp issues before it moves on to the next stage).
+    // Run fn(stage, row scale) on the next stage of the ring once it has
+    // landed (all lanes), then release the slot to the producer warp.
+#ifdef QVL_PERSIST_DETAIL
+    int probe = -1;
+#define PROBE(k) do { if (probe >= 0 && blockIdx.x == 0 && threadIdx.x == 0) S.trace[probe + (k)] = global_ns(); } while (0)
+#else
+#define PROBE(k) do { } while (0)
+#endif
     auto consume = [&](auto &&fn) {
         const int st = cons % kStages;
+        PROBE(0);
         bool ok = tc::mbar_wait(full_bar + 8 * st, (cons / kStages) & 1, S.abort_flag);
         ok = __any_sync(0xffffffffu, ok);          // the phase completes once for all lanes
+        PROBE(1);
         if (ok) fn(ring_ptr + (size_t)st * kStageBytes, ring_scales[st][warp]);
         __syncwarp();
-        // (the slot's values are already consumed by the arithmetic above,
-        // so no fence: a fence here would also wait for this lane's global
-        // stores to complete)
-        if (lane == 0 && atomicAdd(&released[st], 1) == kPWarps - 1) {
-            released[st] = 0;
-            issue_next(prod, W, ring, ring_s, full_bar);
-        }
+        PROBE(2);
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty_bar + 8 * st) : "memory");
         ++cons;
         __syncwarp();
+        PROBE(3);
     };
 
     // Stage RMSNorm weights (int8 -> float, group scales) in shared memory;
@@ -412,16 +489,16 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     auto norm_quant_x = [&](bool inplace_form) {
         for (int i = threadIdx.x; i < H / 4; i += kPThreads)
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.x) + i);
-        __syncthreads();
+        csync();
         if (threadIdx.x < 32) {
             const float ss = rms_sumsq_ref(xs, H);
             if (threadIdx.x == 0) scratch[64] = rms_inv(ss, H, eps, inplace_form);
         }
-        __syncthreads();
+        csync();
         const float inv = scratch[64];
         for (int j = threadIdx.x; j < H; j += kPThreads) ts[j] = mul_rn(nrm_w[j], mul_rn(mul_rn(nrm_s[j / ng], inv), xs[j]));
-        __syncthreads();
-        cta_quantize_smem_row(ts, H, H, q16, &a_s_sh, scratch);
+        csync();
+        quantize_row_smem(ts, H, H, q16, &a_s_sh, scratch);
     };
 
     // embedding_lookup (per-row scale) of the input token into the residual stream
@@ -467,13 +544,13 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         if (l == 5) DETAIL(231);
-        // this CTA's QK-norm weight and RoPE row, read before the barrier
-        const bool qk_cta = blockIdx.x < NH + (pos < S.max_ctx ? NKV : 0);
-        float qk_w = 0.0f, qk_s = 0.0f, rc = 0.0f, rs = 0.0f;
-        if (qk_cta && threadIdx.x < D) {
-            const bool isq = blockIdx.x < NH;
-            qk_w = (float)__ldg((isq ? W.q_norm : W.k_norm) + (size_t)l * D + threadIdx.x);
-            qk_s = __ldg((isq ? W.q_norm_s : W.k_norm_s) + (size_t)l * (D / ng) + threadIdx.x / ng);
+        // QK-norm weights and this position's RoPE row, read before the barrier
+        float qn_w = 0.0f, qn_s = 0.0f, kn_w = 0.0f, kn_s = 0.0f, rc = 0.0f, rs = 0.0f;
+        if (attn_cta && threadIdx.x < D) {
+            qn_w = (float)__ldg(W.q_norm + (size_t)l * D + threadIdx.x);
+            qn_s = __ldg(W.q_norm_s + (size_t)l * (D / ng) + threadIdx.x / ng);
+            kn_w = (float)__ldg(W.k_norm + (size_t)l * D + threadIdx.x);
+            kn_s = __ldg(W.k_norm_s + (size_t)l * (D / ng) + threadIdx.x / ng);
             if (threadIdx.x < D / 2) {
                 rc = __ldg(S.rope_cos + (size_t)pos * (D / 2) + threadIdx.x);
                 rs = __ldg(S.rope_sin + (size_t)pos * (D / 2) + threadIdx.x);
@@ -481,50 +558,61 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         }
         SYNC_OR_EXIT();
 
-        // ---- QK rms_norm_inplace + RoPE (q written back; k, v appended as fp16)
-        // (a position past the cache is not appended; the host keeps pos < max_ctx)
-        if (qk_cta) {
-            const bool isq = blockIdx.x < NH;
-            const int hh = isq ? blockIdx.x : blockIdx.x - NH;
-            const float *src = S.qkv + (isq ? hh * D : NH * D + hh * D);
-            if (threadIdx.x < D) xs[threadIdx.x] = __ldcg(src + threadIdx.x);
-            __syncthreads();
-            if (threadIdx.x < 32) {
-                const float ss = rms_sumsq_ref(xs, D);
-                if (threadIdx.x == 0) scratch[64] = rms_inv(ss, D, eps, true);
+        // ---- attention, phase 1.  q/k rms_norm_inplace + RoPE of this KV
+        // head's two query heads (every slice CTA of the head, redundantly)
+        // and of its key (the CTA whose slice holds the new position, which
+        // appends k and v to the pages as fp16); then the scores of the slice
+        // and their maximum.  (A position past the cache is not appended;
+        // the host keeps pos < max_ctx.)
+        if (attn_cta) {
+            const bool owner = pos < S.max_ctx && t0 <= pos && pos < t1;
+            float *raw = xs;                 // [3][D]: q (2 heads), k
+            float *nrm = xs + 3 * D;         // [3][D] normalised
+            float *qrot = xs + 6 * D;        // [2][D] rotated queries
+            const int rows = owner ? 3 : 2;
+            if (threadIdx.x < rows * D) {
+                const int r = threadIdx.x / D, j = threadIdx.x - r * D;
+                const float *src = r < 2 ? S.qkv + (kvh * 2 + r) * D : S.qkv + NH * D + kvh * D;
+                raw[threadIdx.x] = __ldcg(src + j);
             }
-            __syncthreads();
-            if (threadIdx.x < D) ts[threadIdx.x] = mul_rn(qk_w, mul_rn(mul_rn(qk_s, scratch[64]), xs[threadIdx.x]));
-            __syncthreads();
+            csync();
+            if (warp < rows) {
+                const float ss = rms_sumsq_ref(raw + warp * D, D);
+                if (lane == 0) scratch[warp] = rms_inv(ss, D, eps, true);
+            }
+            csync();
+            if (threadIdx.x < D)
+                for (int r = 0; r < rows; ++r)
+                    nrm[r * D + threadIdx.x] = mul_rn(r < 2 ? qn_w : kn_w,
+                                                      mul_rn(mul_rn(r < 2 ? qn_s : kn_s, scratch[r]), raw[r * D + threadIdx.x]));
+            csync();
             if (threadIdx.x < D / 2) {
                 const int j = threadIdx.x;
-                const float x1 = ts[j], x2 = ts[j + D / 2];
-                const float y1 = fma_rn(x1, rc, -mul_rn(x2, rs));
-                const float y2 = fma_rn(x1, rs, mul_rn(x2, rc));
-                if (isq) {
-                    S.qkv[hh * D + j] = y1;
-                    S.qkv[hh * D + j + D / 2] = y2;
-                } else {
-                    const size_t off = kv_off(S, pt_sm, l, pos, hh);
-                    S.k_pages[off + j] = __half_as_ushort(__float2half_rn(y1));
-                    S.k_pages[off + j + D / 2] = __half_as_ushort(__float2half_rn(y2));
+                for (int r = 0; r < rows; ++r) {
+                    const float x1 = nrm[r * D + j], x2 = nrm[r * D + j + D / 2];
+                    const float y1 = fma_rn(x1, rc, -mul_rn(x2, rs));
+                    const float y2 = fma_rn(x1, rs, mul_rn(x2, rc));
+                    if (r < 2) {
+                        qrot[r * D + j] = y1;
+                        qrot[r * D + j + D / 2] = y2;
+                    } else {
+                        const size_t off = kv_off(S, pt_sm, l, pos, kvh);
+                        S.k_pages[off + j] = __half_as_ushort(__float2half_rn(y1));
+                        S.k_pages[off + j + D / 2] = __half_as_ushort(__float2half_rn(y2));
+                    }
                 }
             }
-            if (!isq && threadIdx.x < D) {
-                const size_t off = kv_off(S, pt_sm, l, pos, hh);
-                S.v_pages[off + threadIdx.x] =
-                    __half_as_ushort(__float2half_rn(__ldcg(S.qkv + NH * D + NKV * D + hh * D + threadIdx.x)));
+            if (owner && threadIdx.x >= D && threadIdx.x < 2 * D) {
+                const int j = threadIdx.x - D;
+                const size_t off = kv_off(S, pt_sm, l, pos, kvh);
+                S.v_pages[off + j] = __half_as_ushort(__float2half_rn(__ldcg(S.qkv + NH * D + NKV * D + kvh * D + j)));
             }
-        }
-        SYNC_OR_EXIT();
-
-        // ---- attention, phase 1: scores of one context slice and its maximum
-        if (attn_cta) {
+            csync();                 // the appended key row is read back below
             float qv[2][8];
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) qv[h][e] = __ldcg(S.qkv + (kvh * 2 + h) * D + t16 * 8 + e);
+                for (int e = 0; e < 8; ++e) qv[h][e] = qrot[h * D + t16 * 8 + e];
             const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
             const unsigned hmask = 0xffffu << (threadIdx.x & 16);
             float mx[2] = {-INFINITY, -INFINITY};
@@ -563,7 +651,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                 if (lane == 0) redf[h][warp] = m;
             }
-            __syncthreads();
+            csync();
             if (threadIdx.x < 2) {
                 float m = redf[threadIdx.x][0];
                 for (int w = 1; w < kPWarps; ++w) m = fmaxf(m, redf[threadIdx.x][w]);
@@ -580,7 +668,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int s2 = 0; s2 < kSlices; ++s2) m = fmaxf(m, __ldcg(S.att_lmax + (kvh * 2 + threadIdx.x) * kSlices + s2));
                 gm[threadIdx.x] = m;
             }
-            __syncthreads();
+            csync();
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 double part = 0.0;
@@ -594,7 +682,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
                 if (lane == 0) redd[h][warp] = part;
             }
-            __syncthreads();
+            csync();
             if (threadIdx.x < 2) {
                 double sum = 0.0;
                 for (int w = 0; w < kPWarps; ++w) sum += redd[threadIdx.x][w];
@@ -633,7 +721,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             for (int h = 0; h < 2; ++h)
 #pragma unroll
                 for (int e = 0; e < 8; ++e) red[(hw * 2 + h) * D + t16 * 8 + e] = acc[h][e];
-            __syncthreads();
+            csync();
             for (int e = threadIdx.x; e < 2 * D; e += kPThreads) {
                 const int h = e / D, dd = e - h * D;
                 float s2 = 0.0f;
@@ -658,15 +746,15 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             head_inv[h] = zero ? 0.0f : (float)(1.0 / sum);
             head_m[h] = zero ? 0.0f : 1.0f;
         }
-        __syncthreads();
+        csync();
         for (int e = threadIdx.x; e < H; e += kPThreads) {
             const int h = e / D, dd = e - h * D;
             float a = 0.0f;
             for (int s2 = 0; s2 < kSlices; ++s2) a += __ldcg(S.att_pacc + (h * kSlices + s2) * D + dd);
             xs[e] = head_m[h] != 0.0f ? mul_rn(a, head_inv[h]) : 0.0f;
         }
-        __syncthreads();
-        cta_quantize_smem_row(xs, H, H, q16, &a_s_sh, scratch);
+        csync();
+        quantize_row_smem(xs, H, H, q16, &a_s_sh, scratch);
         {
             const int nu = cta_units(ph_units(PH_O, W.vocab));
             Act act;
@@ -697,6 +785,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
                 float gate_v = 0.0f;
 #ifdef QVL_PERSIST_DETAIL
+                probe = (l == 5 && j < 2) ? 980 + 16 * j : -1;
                 if (l == 5 && j == 0 && threadIdx.x == 0) {
                     const int st0 = cons % kStages;
                     S.trace[512 + blockIdx.x] = tc::mbar_try_wait(full_bar + 8 * st0, (cons / kStages) & 1) ? 1 : 0;
@@ -708,6 +797,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                     gate_v = finish_row(p, a_s_sh, sc, lane);
                 });
 #ifdef QVL_PERSIST_DETAIL
+                if (probe >= 0) probe += 8;
+#endif
+#ifdef QVL_PERSIST_DETAIL
                 if (l == 5 && j == 0 && threadIdx.x == 0) S.trace[822 + blockIdx.x] = global_ns();
 #endif
                 consume([&](const unsigned char *st, float sc) {
@@ -716,6 +808,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                     const float up = finish_row(p, a_s_sh, sc, lane);
                     if (lane == 0) S.h[n] = swiglu_one(gate_v, up);
                 });
+#ifdef QVL_PERSIST_DETAIL
+                probe = -1;
+#endif
                 if (l == 5) DETAIL(234 + j);
 #ifdef QVL_PERSIST_DETAIL
                 if (l == 5 && threadIdx.x == 0 && j < 2) { if (j == 0) S.trace[672 + blockIdx.x] = global_ns(); }
@@ -731,8 +826,8 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         // ---- quantisation of the SwiGLU row (every CTA), down + residual
         for (int i = threadIdx.x; i < I / 4; i += kPThreads)
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.h) + i);
-        __syncthreads();
-        cta_quantize_smem_row(xs, I, I, q16, &a_s_sh, scratch);
+        csync();
+        quantize_row_smem(xs, I, I, q16, &a_s_sh, scratch);
         {
             const int nu = cta_units(ph_units(PH_DOWN, W.vocab));
             for (int j = 0; j < nu; ++j) {
@@ -800,7 +895,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             if (v2 > v || (v2 == v && i2 < bi)) { v = v2; bi = i2; }
         }
         if (lane == 0) { redf[0][warp] = v; reinterpret_cast<int *>(scratch)[warp] = bi; }
-        __syncthreads();
+        csync();
         if (threadIdx.x == 0) {
             float fv = -FLT_MAX;
             int fi = INT_MAX;
@@ -826,7 +921,7 @@ int persist_grid_ctas() {
     if (cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)persist_smem_bytes()) != cudaSuccess)
         return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_persistent_kernel, kPThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_persistent_kernel, kBlock,
                                                       persist_smem_bytes()) != cudaSuccess)
         return 0;
     // every attention (KV head, slice) pair and QK row needs a CTA of its own
@@ -844,7 +939,7 @@ bool persist_supported(int hidden, int intermediate, int heads, int kv_heads, in
 cudaError_t launch_decode_persistent(const PersistWeights &w, const PersistState &s, int ctas, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas);
-    cfg.blockDim = dim3(kPThreads);
+    cfg.blockDim = dim3(kBlock);
     cfg.dynamicSmemBytes = persist_smem_bytes();
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
