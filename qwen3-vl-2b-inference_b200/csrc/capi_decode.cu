@@ -10,7 +10,7 @@ constexpr size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 // Workspace layout; the barrier words come first so that they keep their
 // place whatever the device's SM count.
 struct DecodeWs {
-    size_t bar, trace, x_qkv, h, lmax, lsum, pacc, best_v, best_i, total;
+    size_t bar, trace, x_qkv, h, lmax, lsum, pacc, cnt, att, best_v, best_i, total;
 };
 constexpr DecodeWs decode_ws() {
     DecodeWs w{};
@@ -21,7 +21,9 @@ constexpr DecodeWs decode_ws() {
     w.lmax = w.h + al256(6144 * 4);
     w.lsum = w.lmax + al256(16 * qvl::kPersistSlices * 4);
     w.pacc = w.lsum + al256(16 * qvl::kPersistSlices * 8);
-    w.best_v = w.pacc + al256(16 * qvl::kPersistSlices * 128 * 4);
+    w.cnt = w.pacc + al256(16 * qvl::kPersistSlices * 128 * 4);
+    w.att = w.cnt + 256;
+    w.best_v = w.att + al256(16 * 128 * 4);
     w.best_i = w.best_v + al256(kMaxCtas * qvl::kPersistWarpsPerCta * 4);
     w.total = w.best_i + al256(kMaxCtas * qvl::kPersistWarpsPerCta * 4);
     return w;
@@ -94,6 +96,8 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
     ps.att_lmax = reinterpret_cast<float *>(ws + L.lmax);
     ps.att_lsum = reinterpret_cast<double *>(ws + L.lsum);
     ps.att_pacc = reinterpret_cast<float *>(ws + L.pacc);
+    ps.att_cnt = reinterpret_cast<int *>(ws + L.cnt);
+    ps.att_out = reinterpret_cast<float *>(ws + L.att);
     ps.warp_best_v = reinterpret_cast<float *>(ws + L.best_v);
     ps.warp_best_i = reinterpret_cast<int *>(ws + L.best_i);
     ps.token = token;

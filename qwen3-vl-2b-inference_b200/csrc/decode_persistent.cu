@@ -390,8 +390,8 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     __shared__ float scratch[65];
     __shared__ float a_s_sh;
     __shared__ int aborted_at_entry;
+    __shared__ int last_cta;
     __shared__ int pt_sm[kMaxPages];
-    __shared__ float head_m[NH], head_inv[NH];
     __shared__ float redf[2][kPWarps];
     __shared__ double redd[2][kPWarps];
 
@@ -486,19 +486,23 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     // x (residual, written by other CTAs) -> RMSNorm with the staged weight
     // -> quantisation (one scale) into q16 / a_s_sh; arithmetic of
     // cta_norm_quant_row.
-    auto norm_quant_x = [&](bool inplace_form) {
+    auto norm_quant_x = [&](bool inplace_form, int dbg = -1) {
         for (int i = threadIdx.x; i < H / 4; i += kPThreads)
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.x) + i);
         csync();
+        if (dbg >= 0) DETAIL(dbg);
         if (threadIdx.x < 32) {
             const float ss = rms_sumsq_ref(xs, H);
             if (threadIdx.x == 0) scratch[64] = rms_inv(ss, H, eps, inplace_form);
         }
         csync();
+        if (dbg >= 0) DETAIL(dbg + 1);
         const float inv = scratch[64];
         for (int j = threadIdx.x; j < H; j += kPThreads) ts[j] = mul_rn(nrm_w[j], mul_rn(mul_rn(nrm_s[j / ng], inv), xs[j]));
         csync();
+        if (dbg >= 0) DETAIL(dbg + 2);
         quantize_row_smem(ts, H, H, q16, &a_s_sh, scratch);
+        if (dbg >= 0) DETAIL(dbg + 3);
     };
 
     // embedding_lookup (per-row scale) of the input token into the residual stream
@@ -527,7 +531,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         // ---- input rms_norm + quantisation (every CTA), q/k/v blocks of the ring
-        norm_quant_x(false);
+        norm_quant_x(false, l == 5 ? 240 : -1);
         if (l == 5) DETAIL(230);
         {
             const int nu = cta_units(ph_units(PH_QKV, W.vocab));
@@ -728,33 +732,55 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 0; w < 32; ++w) s2 += red[(w * 2 + h) * D + dd];
                 S.att_pacc[((kvh * 2 + h) * kSlices + sl) * D + dd] = s2;
             }
+            // The last of the head's 16 slice CTAs to finish combines its two
+            // query heads (softmax normalisation included) into att_out, so
+            // that the o_proj phase reads 8 KB instead of every partial.
+            __threadfence();
+            csync();
+            if (threadIdx.x == 0) last_cta = atomicAdd(S.att_cnt + kvh, 1) == kSlices - 1;
+            csync();
+            if (last_cta) {
+                __threadfence();
+                if (threadIdx.x < 2 * D / 4) {
+                    const int e0 = threadIdx.x * 4, head = kvh * 2 + e0 / D, dd = e0 % D;
+                    float4 pv[kSlices];
+                    float lm[kSlices];
+                    double ls[kSlices];
+#pragma unroll
+                    for (int s2 = 0; s2 < kSlices; ++s2) {
+                        pv[s2] = __ldcg(reinterpret_cast<const float4 *>(S.att_pacc + (head * kSlices + s2) * D + dd));
+                        lm[s2] = __ldcg(S.att_lmax + head * kSlices + s2);
+                        ls[s2] = __ldcg(S.att_lsum + head * kSlices + s2);
+                    }
+                    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    float m = -INFINITY;
+                    double sum = 0.0;
+#pragma unroll
+                    for (int s2 = 0; s2 < kSlices; ++s2) {
+                        a.x += pv[s2].x; a.y += pv[s2].y; a.z += pv[s2].z; a.w += pv[s2].w;
+                        m = fmaxf(m, lm[s2]);
+                        sum += ls[s2];
+                    }
+                    // the reference zeroes the row when the max is not finite or the
+                    // sum is not a positive finite number (text_layer.cpp:466-469, :514-517)
+                    const bool zero = ctx <= 0 || !isfinite(m) || !(sum > 0.0) || !isfinite(sum);
+                    const float inv = zero ? 0.0f : (float)(1.0 / sum);
+                    reinterpret_cast<float4 *>(S.att_out)[(head * D + dd) / 4] =
+                        zero ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                             : make_float4(mul_rn(a.x, inv), mul_rn(a.y, inv), mul_rn(a.z, inv), mul_rn(a.w, inv));
+                }
+                if (threadIdx.x == 0) S.att_cnt[kvh] = 0;     // next used a grid barrier later
+            }
         }
         SYNC_OR_EXIT();
 
-        // ---- attention combine (every CTA) -> quantisation -> o_proj + residual
-        if (threadIdx.x < NH) {
-            const int h = threadIdx.x;
-            float m = -INFINITY;
-            double sum = 0.0;
-            for (int s2 = 0; s2 < kSlices; ++s2) {
-                m = fmaxf(m, __ldcg(S.att_lmax + h * kSlices + s2));
-                sum += __ldcg(S.att_lsum + h * kSlices + s2);
-            }
-            // the reference zeroes the row when the max is not finite or the
-            // sum is not a positive finite number (text_layer.cpp:466-469, :514-517)
-            const bool zero = ctx <= 0 || !isfinite(m) || !(sum > 0.0) || !isfinite(sum);
-            head_inv[h] = zero ? 0.0f : (float)(1.0 / sum);
-            head_m[h] = zero ? 0.0f : 1.0f;
-        }
+        // ---- attention output (combined above) -> quantisation -> o_proj + residual
+        for (int i = threadIdx.x; i < H / 4; i += kPThreads)
+            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.att_out) + i);
         csync();
-        for (int e = threadIdx.x; e < H; e += kPThreads) {
-            const int h = e / D, dd = e - h * D;
-            float a = 0.0f;
-            for (int s2 = 0; s2 < kSlices; ++s2) a += __ldcg(S.att_pacc + (h * kSlices + s2) * D + dd);
-            xs[e] = head_m[h] != 0.0f ? mul_rn(a, head_inv[h]) : 0.0f;
-        }
-        csync();
+        if (l == 5) DETAIL(245);
         quantize_row_smem(xs, H, H, q16, &a_s_sh, scratch);
+        if (l == 5) DETAIL(246);
         {
             const int nu = cta_units(ph_units(PH_O, W.vocab));
             Act act;
@@ -770,6 +796,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 });
             }
         }
+        if (l == 5) DETAIL(247);
         stage_norm(W.post_norm + (size_t)l * H, W.post_norm_s + (size_t)l * (H / ng));
         SYNC_OR_EXIT();
 

@@ -27,6 +27,8 @@ struct PersistState {
     float *att_lmax;       // [NH][16] slice maxima
     double *att_lsum;      // [NH][16] slice sums
     float *att_pacc;       // [NH][16][D] slice partial outputs
+    int *att_cnt;          // [NKV] slices finished (zero between layers)
+    float *att_out;        // [NH * D] attention output
     float *warp_best_v;    // [grid * 16]
     int *warp_best_i;      // [grid * 16]
     int32_t *token;        // [1] input token, replaced by the greedy token

@@ -13,10 +13,14 @@ __device__ __forceinline__ float inv127() { return __int_as_float(0x3c010204); }
 // of the half-warp, broadcast to all 16.
 __device__ __forceinline__ float group_sumsq_ref(const float *xg, int g, int t16) {
     float acc = 0.0f;
-#pragma unroll 16
-    for (int j = 0; j < g; j += 16) {
-        float v = xg[j + t16];
-        acc = fma_rn(v, v, acc);
+    // values of a batch are loaded ahead of the (serial) fma chain
+    for (int j0 = 0; j0 < g; j0 += 16 * 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = j0 + 16 * k < g ? xg[j0 + 16 * k + t16] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (j0 + 16 * k < g) acc = fma_rn(v[k], v[k], acc);
     }
     const unsigned full = 0xffffffffu;
     float o = __shfl_down_sync(full, acc, 8, 16);

@@ -15,10 +15,18 @@ namespace qvl {
 __device__ __forceinline__ float rms_sumsq_ref(const float *xs, int H) {
     const int l = threadIdx.x & 7;
     float acc = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < H; i += 8) {
-        const float v = xs[i + l];
-        acc = add_rn(acc, mul_rn(v, v));
+    // squares of a batch are loaded and formed ahead of the (serial) sum
+    for (int i0 = 0; i0 < H; i0 += 8 * 32) {
+        float sq[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            const int i = i0 + 8 * k;
+            const float v = i < H ? xs[i + l] : 0.0f;
+            sq[k] = mul_rn(v, v);
+        }
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            if (i0 + 8 * k < H) acc = add_rn(acc, sq[k]);
     }
     float ss = 0.0f;
 #pragma unroll
