@@ -233,7 +233,7 @@ struct Producer {
 // Issue the next stage of the stream into its ring slot (whose previous
 // contents every warp has released), if the stream has one left.
 __device__ __forceinline__ void issue_next(Producer &p, const PersistWeights &W, uint32_t ring, uint32_t ring_s,
-                                           uint32_t full_bar, unsigned long long *dbg = nullptr) {
+                                           uint32_t full_bar) {
     if (p.c.ph == PH_DONE) return;
     const int st = p.issued % kStages;
     size_t stride;
@@ -241,17 +241,14 @@ __device__ __forceinline__ void issue_next(Producer &p, const PersistWeights &W,
     const float *ssrc = cursor_scales(p.c, W);
     const uint32_t bar = full_bar + 8 * st;
     const uint32_t dst = ring + (uint32_t)st * kStageBytes;
-    if (dbg) dbg[0] = global_ns();
     tc::mbar_expect_tx(bar, kStageBytes + kRows * 4);
     bulk_g2s(ring_s + (uint32_t)st * kRows * 4, ssrc, kRows * 4, bar, p.policy);
-    if (dbg) dbg[1] = global_ns();
     if (stride == kSegBytes) {
         bulk_g2s(dst, src, kStageBytes, bar, p.policy);
     } else {
 #pragma unroll 1
         for (int r = 0; r < kRows; ++r) bulk_g2s(dst + r * kSegBytes, src + (size_t)r * stride, kSegBytes, bar, p.policy);
     }
-    if (dbg) dbg[2] = global_ns();
     ++p.issued;
     cursor_next(p.c, W.layers, p.cnt);
 }
@@ -455,25 +452,15 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
 
     // Run fn(stage, row scale) on the next stage of the ring once it has
     // landed (all lanes), then release the slot to the producer warp.
-#ifdef QVL_PERSIST_DETAIL
-    int probe = -1;
-#define PROBE(k) do { if (probe >= 0 && blockIdx.x == 0 && threadIdx.x == 0) S.trace[probe + (k)] = global_ns(); } while (0)
-#else
-#define PROBE(k) do { } while (0)
-#endif
     auto consume = [&](auto &&fn) {
         const int st = cons % kStages;
-        PROBE(0);
         bool ok = tc::mbar_wait(full_bar + 8 * st, (cons / kStages) & 1, S.abort_flag);
         ok = __any_sync(0xffffffffu, ok);          // the phase completes once for all lanes
-        PROBE(1);
         if (ok) fn(ring_ptr + (size_t)st * kStageBytes, ring_scales[st][warp]);
         __syncwarp();
-        PROBE(2);
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty_bar + 8 * st) : "memory");
         ++cons;
         __syncwarp();
-        PROBE(3);
     };
 
     // Stage RMSNorm weights (int8 -> float, group scales) in shared memory;
@@ -808,46 +795,27 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             const int nu = cta_units(ph_units(PH_GU, W.vocab));
             Act act;
             load_act(q_s, 0, lane, act);
+            // lane j keeps unit j's gate/up pair; the SwiGLUs (double-precision
+            // exp) run once, in parallel, after the last unit
+            float g_keep = 0.0f, u_keep = 0.0f;
             for (int j = 0; j < nu; ++j) {
-                const int n = ((int)blockIdx.x + j * (int)gridDim.x) * kRows + warp;
                 float gate_v = 0.0f;
-#ifdef QVL_PERSIST_DETAIL
-                probe = (l == 5 && j < 2) ? 980 + 16 * j : -1;
-                if (l == 5 && j == 0 && threadIdx.x == 0) {
-                    const int st0 = cons % kStages;
-                    S.trace[512 + blockIdx.x] = tc::mbar_try_wait(full_bar + 8 * st0, (cons / kStages) & 1) ? 1 : 0;
-                }
-#endif
                 consume([&](const unsigned char *st, float sc) {
                     int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     madd_seg(st, warp, lane, act, p);
                     gate_v = finish_row(p, a_s_sh, sc, lane);
                 });
-#ifdef QVL_PERSIST_DETAIL
-                if (probe >= 0) probe += 8;
-#endif
-#ifdef QVL_PERSIST_DETAIL
-                if (l == 5 && j == 0 && threadIdx.x == 0) S.trace[822 + blockIdx.x] = global_ns();
-#endif
                 consume([&](const unsigned char *st, float sc) {
                     int p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     madd_seg(st, warp, lane, act, p);
                     const float up = finish_row(p, a_s_sh, sc, lane);
-                    if (lane == 0) S.h[n] = swiglu_one(gate_v, up);
+                    if (lane == j) { g_keep = gate_v; u_keep = up; }
                 });
-#ifdef QVL_PERSIST_DETAIL
-                probe = -1;
-#endif
-                if (l == 5) DETAIL(234 + j);
-#ifdef QVL_PERSIST_DETAIL
-                if (l == 5 && threadIdx.x == 0 && j < 2) { if (j == 0) S.trace[672 + blockIdx.x] = global_ns(); }
-#endif
             }
+            if (lane < nu) S.h[((int)blockIdx.x + lane * (int)gridDim.x) * kRows + warp] = swiglu_one(g_keep, u_keep);
         }
         if (l == 5) DETAIL(233);
-#ifdef QVL_PERSIST_DETAIL
-        if (l == 5 && threadIdx.x == 0) S.trace[256 + blockIdx.x] = global_ns();
-#endif
+
         SYNC_OR_EXIT();
 
         // ---- quantisation of the SwiGLU row (every CTA), down + residual
