@@ -289,24 +289,25 @@ __device__ __noinline__ void produce(Producer &p, const PersistWeights &W, uint3
     *reinterpret_cast<volatile int *>(done) = 1;
 }
 
-// cta_quantize_smem_row for the compute warps (named barrier, kPThreads):
-// group scales of ts[0..n) (group g, n / g <= 64) and quantisation into q.
-__device__ __forceinline__ void quantize_row_smem(const float *ts, int n, int g, int16_t *q, float *qs,
-                                                  float *scratch) {
-    const int G = n / g;
-    const int hw = threadIdx.x >> 4, nhw = kPThreads >> 4, t16 = threadIdx.x & 15;
-    for (int e0 = hw & ~1; e0 < G; e0 += nhw) {   // both half-warps of a warp take the same trip count
-        const int e_raw = e0 + (hw & 1);
-        const bool active = e_raw < G;
-        const int e = active ? e_raw : e0;
-        const float sc = group_scale_ref(ts + (size_t)e * g, g, t16);
-        if (active && t16 == 0) {
-            qs[e] = sc;
-            scratch[e] = __fdiv_rn(1.0f, sc);
+// Quantisation of one whole row of N values (a single group, the per-row
+// scale of the reference's activation quantisation) by the compute warps:
+// warp 0 forms the scale (group_scale_ref; both half-warps compute
+// it, so the full-mask shuffles of the reduction see all 32 lanes), then
+// every thread quantises its elements.
+template <int N>
+__device__ __forceinline__ void quantize_row_n(const float *ts, int16_t *q, float *qs, float *scratch) {
+    if (threadIdx.x < 32) {
+        const float ss = group_sumsq_ref(ts, N, threadIdx.x & 15);
+        const float sc = mul_rn(__fsqrt_rn(fma_rn(ss, __fdiv_rn(1.0f, (float)N), 1e-6f)), inv127());
+        if (threadIdx.x == 0) {
+            *qs = sc;
+            scratch[0] = __fdiv_rn(1.0f, sc);
         }
     }
     csync();
-    for (int j = threadIdx.x; j < n; j += kPThreads) q[j] = quant_one(ts[j], scratch[j / g]);
+    const float inv = scratch[0];
+#pragma unroll
+    for (int j = threadIdx.x; j < N; j += kPThreads) q[j] = quant_one(ts[j], inv);
     csync();
 }
 
@@ -488,7 +489,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         for (int j = threadIdx.x; j < H; j += kPThreads) ts[j] = mul_rn(nrm_w[j], mul_rn(mul_rn(nrm_s[j / ng], inv), xs[j]));
         csync();
         if (dbg >= 0) DETAIL(dbg + 2);
-        quantize_row_smem(ts, H, H, q16, &a_s_sh, scratch);
+        quantize_row_n<H>(ts, q16, &a_s_sh, scratch);
         if (dbg >= 0) DETAIL(dbg + 3);
     };
 
@@ -766,7 +767,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.att_out) + i);
         csync();
         if (l == 5) DETAIL(245);
-        quantize_row_smem(xs, H, H, q16, &a_s_sh, scratch);
+        quantize_row_n<H>(xs, q16, &a_s_sh, scratch);
         if (l == 5) DETAIL(246);
         {
             const int nu = cta_units(ph_units(PH_O, W.vocab));
@@ -822,7 +823,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         for (int i = threadIdx.x; i < I / 4; i += kPThreads)
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.h) + i);
         csync();
-        quantize_row_smem(xs, I, I, q16, &a_s_sh, scratch);
+        quantize_row_n<I>(xs, q16, &a_s_sh, scratch);
         {
             const int nu = cta_units(ph_units(PH_DOWN, W.vocab));
             for (int j = 0; j < nu; ++j) {

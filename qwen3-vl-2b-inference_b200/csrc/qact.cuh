@@ -11,6 +11,21 @@ __device__ __forceinline__ float inv127() { return __int_as_float(0x3c010204); }
 
 // Sum of squares of one group in the reference order; valid in lane t16 == 0
 // of the half-warp, broadcast to all 16.
+// The reference's reduction of the 16 lane sums of a group (lane order of
+// _mm256 pairs, then (u0+u1)+(u2+u3)); the result is broadcast to all 16.
+__device__ __forceinline__ float group_reduce16_ref(float acc) {
+    const unsigned full = 0xffffffffu;
+    float o = __shfl_down_sync(full, acc, 8, 16);
+    float v = add_rn(acc, o);                     // lane l<8: v_l = a0_l + a1_l
+    o = __shfl_down_sync(full, v, 4, 16);
+    float u = add_rn(v, o);                       // l<4: u_l = v_l + v_{l+4}
+    o = __shfl_down_sync(full, u, 1, 16);
+    float p = add_rn(u, o);                       // l=0: u0+u1 ; l=2: u2+u3
+    o = __shfl_down_sync(full, p, 2, 16);
+    float r = add_rn(p, o);                       // l=0: (u0+u1)+(u2+u3)
+    return __shfl_sync(full, r, 0, 16);
+}
+
 __device__ __forceinline__ float group_sumsq_ref(const float *xg, int g, int t16) {
     float acc = 0.0f;
     // values of a batch are loaded ahead of the (serial) fma chain
@@ -22,16 +37,7 @@ __device__ __forceinline__ float group_sumsq_ref(const float *xg, int g, int t16
         for (int k = 0; k < 16; ++k)
             if (j0 + 16 * k < g) acc = fma_rn(v[k], v[k], acc);
     }
-    const unsigned full = 0xffffffffu;
-    float o = __shfl_down_sync(full, acc, 8, 16);
-    float v = add_rn(acc, o);                     // lane l<8: v_l = a0_l + a1_l
-    o = __shfl_down_sync(full, v, 4, 16);
-    float u = add_rn(v, o);                       // l<4: u_l = v_l + v_{l+4}
-    o = __shfl_down_sync(full, u, 1, 16);
-    float p = add_rn(u, o);                       // l=0: u0+u1 ; l=2: u2+u3
-    o = __shfl_down_sync(full, p, 2, 16);
-    float r = add_rn(p, o);                       // l=0: (u0+u1)+(u2+u3)
-    return __shfl_sync(full, r, 0, 16);
+    return group_reduce16_ref(acc);
 }
 
 __device__ __forceinline__ int16_t quant_one(float x, float inv) {
