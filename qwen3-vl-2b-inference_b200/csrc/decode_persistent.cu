@@ -98,13 +98,20 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // barrier (the CTA's writes are ordered by bar.sync, then published by the
 // release).  Returns false if the wait gave up or another CTA aborted.
 // CTA 0 records the time each barrier opens in S.trace[1 + k].
-__device__ __forceinline__ bool grid_sync(const PersistState &S, int &nsync) {
+// Split into arrive and wait so that a CTA can load constants of the next
+// phase (norm weights, RoPE row) while the barrier completes.
+__device__ __forceinline__ void grid_arrive(const PersistState &S, unsigned long long &target) {
     csync();
+    if (threadIdx.x == 0) {
+        unsigned long long old;
+        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.bar_count) : "memory");
+        target = (old / gridDim.x + 1) * gridDim.x;
+    }
+}
+__device__ __forceinline__ bool grid_wait(const PersistState &S, unsigned long long target, int &nsync) {
     __shared__ int ok;
     if (threadIdx.x == 0) {
-        unsigned long long old, v;
-        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.bar_count) : "memory");
-        const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+        unsigned long long v;
         int good = 1;
         asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.bar_count) : "memory");
         if (v < target) {
@@ -446,9 +453,16 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
 #else
 #define DETAIL(slot) do { } while (0)
 #endif
+    unsigned long long bar_target = 0;       // thread 0: arrivals that complete the current barrier
+#define GRID_ARRIVE() grid_arrive(S, bar_target)
+#define GRID_WAIT_OR_EXIT()                                                               \
+    do {                                                                                  \
+        if (!grid_wait(S, bar_target, nsync)) { drain(); return; }                        \
+    } while (0)
 #define SYNC_OR_EXIT()                                                                    \
     do {                                                                                  \
-        if (!grid_sync(S, nsync)) { drain(); return; }                                    \
+        GRID_ARRIVE();                                                                    \
+        GRID_WAIT_OR_EXIT();                                                              \
     } while (0)
 
     // Run fn(stage, row scale) on the next stage of the ring once it has
@@ -499,8 +513,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         const float sc = W.embed_s[id];
         for (int j = threadIdx.x; j < H; j += kPThreads) S.x[j] = mul_rn((float)W.embed[(size_t)id * H + j], sc);
     }
+    GRID_ARRIVE();
     stage_norm(W.in_norm, W.in_norm_s);
-    SYNC_OR_EXIT();
+    GRID_WAIT_OR_EXIT();
 
     const int per = (ctx + kSlices - 1) / kSlices;
     const bool attn_cta = blockIdx.x < NKV * kSlices;
@@ -536,7 +551,8 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         if (l == 5) DETAIL(231);
-        // QK-norm weights and this position's RoPE row, read before the barrier
+        GRID_ARRIVE();
+        // QK-norm weights and this position's RoPE row, read while the barrier completes
         float qn_w = 0.0f, qn_s = 0.0f, kn_w = 0.0f, kn_s = 0.0f, rc = 0.0f, rs = 0.0f;
         if (attn_cta && threadIdx.x < D) {
             qn_w = (float)__ldg(W.q_norm + (size_t)l * D + threadIdx.x);
@@ -548,7 +564,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 rs = __ldg(S.rope_sin + (size_t)pos * (D / 2) + threadIdx.x);
             }
         }
-        SYNC_OR_EXIT();
+        GRID_WAIT_OR_EXIT();
 
         // ---- attention, phase 1.  q/k rms_norm_inplace + RoPE of this KV
         // head's two query heads (every slice CTA of the head, redundantly)
@@ -785,8 +801,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         if (l == 5) DETAIL(247);
+        GRID_ARRIVE();
         stage_norm(W.post_norm + (size_t)l * H, W.post_norm_s + (size_t)l * (H / ng));
-        SYNC_OR_EXIT();
+        GRID_WAIT_OR_EXIT();
 
         // ---- post-attention rms_norm + quantisation (every CTA), gate/up + SwiGLU
         norm_quant_x(false);
@@ -842,9 +859,10 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 if (lane == 0) S.x[n] = add_rn(xn, out);
             }
         }
+        GRID_ARRIVE();
         if (l + 1 < W.layers) stage_norm(W.in_norm + (size_t)(l + 1) * H, W.in_norm_s + (size_t)(l + 1) * (H / ng));
         else stage_norm(W.final_norm, W.final_norm_s);
-        SYNC_OR_EXIT();
+        GRID_WAIT_OR_EXIT();
     }
 
     // ---- final rms_norm_inplace + quantisation (every CTA), LM head + greedy
