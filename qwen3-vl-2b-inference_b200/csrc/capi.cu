@@ -2,11 +2,13 @@
 // workspace carving and kernel sequencing.  No entry point allocates memory,
 // synchronises the stream, exits or traps.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include "common.cuh"
 #include "qact.cuh"
 #include "gemv_i8.cuh"
 #include "gemm_i8_tc.cuh"
+#include "gemv_ring.cuh"
 #include "swiglu.cuh"
 #include "attention.cuh"
 #include "argmax.cuh"
@@ -30,6 +32,19 @@ int gemv_rows_per_launch(size_t K, size_t g) {
     return 0;
 }
 
+// Single-row per-row-scale GEMVs of at least this many weight bytes stream
+// through the ring kernel (gemv_ring.cu); smaller ones keep the direct-load
+// kernel.  QVL_GEMV_RING=0 in the environment disables the ring kernel.
+constexpr size_t kRingMinBytes = 4u << 20;
+bool ring_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("QVL_GEMV_RING");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 bool lane8_for(int semantics, size_t M, size_t N, size_t K) {
     if (semantics == QVL_SEM_LANE8) return true;
     if (semantics == QVL_SEM_TILED) return false;
@@ -48,6 +63,13 @@ int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const flo
         uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, K) / 2;
         QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, hi, lo, B, Bs, C, (int)M, (int)N, (int)K, st));
         return QVL_OK;
+    }
+    if (M == 1 && lane8 && g == K && N * K >= kRingMinBytes && ring_enabled()) {
+        qvl::RingGemvArgs r{q, qs, B, Bs, C, (int)N, (int)K, acc};
+        if (qvl::gemv_ring_supported(r)) {
+            QVL_CUDA_TRY(qvl::launch_gemv_ring(r, st));
+            return QVL_OK;
+        }
     }
     const int mr = gemv_rows_per_launch(K, g);
     if (mr == 0) return QVL_ERR_UNSUPPORTED;

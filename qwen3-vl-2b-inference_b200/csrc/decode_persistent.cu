@@ -36,14 +36,15 @@
 #include "gemv_common.cuh"
 #include "tail.cuh"
 #include "tc_common.cuh"
+#include "ring_common.cuh"
 #include "decode_persistent.cuh"
 
 namespace qvl {
 
 namespace {
-constexpr int kPThreads = 512;                 // compute threads (16 warps)
-constexpr int kPWarps = kPThreads / 32;
-constexpr int kBlock = kPThreads + 32;         // + one producer warp that feeds the weight ring
+using namespace ring;
+constexpr int kPThreads = ring::kThreads;      // compute threads (16 warps)
+constexpr int kPWarps = ring::kWarps;
 constexpr int H = 2048, I = 6144, NH = 16, NKV = 8, D = 128;
 constexpr int kSlices = kPersistSlices;        // attention context slices per KV head
 constexpr int kSliceMax = 512;                 // tokens per slice (context <= 8192)
@@ -51,10 +52,7 @@ constexpr int kMaxPages = kSlices * kSliceMax / 16;   // page table entries (pag
 constexpr unsigned long long kBarrierLimitNs = 2000000000ull;
 constexpr unsigned kTraceSlots = kPersistTraceSlots;
 
-// weight ring: a stage is 16 row segments of 2048 bytes, one per warp
-constexpr int kRows = kPWarps;
-constexpr int kSegBytes = 2048;
-constexpr int kStageBytes = kRows * kSegBytes;
+// weight ring: kStages stages of 16 row segments of 2048 bytes, one per warp
 constexpr int kStages = 5;
 
 // dynamic shared memory: ring | q16 [I] int16 | xs [I] f32 | ts [H] f32 | sp [2][kSliceMax] f32 |
@@ -81,16 +79,6 @@ __device__ __forceinline__ int cta_units(int U) {
 __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
     return *reinterpret_cast<const volatile unsigned *>(p);
 }
-// Barrier of the 16 compute warps only (named barrier 1); the producer warp
-// never joins it.
-__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kPThreads) : "memory"); }
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
 // Grid barrier with a bounded wait.  The counter only grows (it is zero
 // when the workspace is cleared), so barrier k of a launch completes when
 // the arrivals reach the next multiple of gridDim.x: no reset, no second
@@ -152,20 +140,6 @@ __device__ __forceinline__ size_t kv_off(const PersistState &S, const int *pt, i
     const int page = pt[t / S.page_size];
     const int slot = t - (t / S.page_size) * S.page_size;
     return (size_t)layer * S.kv_layer_stride + (((size_t)page * NKV + kvh) * S.page_size + slot) * D;
-}
-
-// ---------------------------------------------------------------- weight ring
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
-                                         uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
 }
 
 // Position in this CTA's stream: layer, matrix phase, unit index j, stage s.
@@ -318,61 +292,6 @@ __device__ __forceinline__ void quantize_row_n(const float *ts, int16_t *q, floa
     csync();
 }
 
-// This lane's activation chunks [cbase, cbase + 128) of q_s (int16 pairs),
-// held in registers for every row of a phase.
-struct Act {
-    int4 a[8];
-};
-__device__ __forceinline__ void load_act(const int4 *q_s, int cbase, int lane, Act &act) {
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-        const int c = cbase + it * 32 + lane;
-        act.a[2 * it] = q_s[2 * c];
-        act.a[2 * it + 1] = q_s[2 * c + 1];
-    }
-}
-
-// int32 lane sums of one 2048-byte row segment (this warp's row of a stage)
-// against the register-held activation chunks.
-__device__ __forceinline__ void madd_seg(const unsigned char *stage, int warp, int lane, const Act &act, int p[8]) {
-    const uint4 *row = reinterpret_cast<const uint4 *>(stage + warp * kSegBytes);
-    uint4 w[4];
-#pragma unroll
-    for (int it = 0; it < 4; ++it) w[it] = row[it * 32 + lane];
-#pragma unroll
-    for (int it = 0; it < 4; ++it) madd_chunk(w[it], act.a[2 * it], act.a[2 * it + 1], p);
-}
-
-// Row result from the int32 lane sums, in the reference's 8-lane order
-// (cpu_f32a_i8f32sb_f32c_avx2.cpp:181-223): lane sums reduced over the warp,
-// each lane's sum scaled (one group: the whole row), lanes added pairwise.
-// Valid in all lanes.
-__device__ __forceinline__ float finish_row(int (&p)[8], float a_s, float w_s, int lane) {
-    const unsigned full = 0xffffffffu;
-    bool up = lane & 16;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int send = up ? p[i] : p[i + 4];
-        int keep = up ? p[i + 4] : p[i];
-        p[i] = keep + __shfl_xor_sync(full, send, 16);
-    }
-    up = lane & 8;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        int send = up ? p[i] : p[i + 2];
-        int keep = up ? p[i + 2] : p[i];
-        p[i] = keep + __shfl_xor_sync(full, send, 8);
-    }
-    up = lane & 4;
-    int r = (up ? p[1] : p[0]) + __shfl_xor_sync(full, up ? p[0] : p[1], 4);
-    r += __shfl_xor_sync(full, r, 2);
-    r += __shfl_xor_sync(full, r, 1);
-    const float cf = fma_rn(__int2float_rn(r), mul_rn(a_s, w_s), 0.0f);
-    const float u = add_rn(cf, __shfl_xor_sync(full, cf, 16));
-    const float pp = add_rn(u, __shfl_xor_sync(full, u, 4));
-    return add_rn(pp, __shfl_xor_sync(full, pp, 8));
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kBlock, 1)
@@ -473,7 +392,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         ok = __any_sync(0xffffffffu, ok);          // the phase completes once for all lanes
         if (ok) fn(ring_ptr + (size_t)st * kStageBytes, ring_scales[st][warp]);
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty_bar + 8 * st) : "memory");
+        if (lane == 0) mbar_arrive(empty_bar + 8 * st);
         ++cons;
         __syncwarp();
     };

@@ -104,6 +104,21 @@ def test_lm_head_gemv(qvl, cuda):
     assert int(idx.item()) == oracle.argmax(yo[0])
 
 
+@pytest.mark.parametrize("N,K", [(4096, 2048), (2048, 6144), (16, 2048)])
+def test_ring_gemv_accumulate(qvl, cuda, N, K):
+    """M=1 per-row GEMVs of >= 4 MiB stream through the ring kernel (the
+    16-row case stays on the direct-load kernel): C += x.W^T bit-exact
+    against the reference's product plus the separate add (add_vector)."""
+    import torch
+    x, w, ws = make_linear_inputs(321 + N + K, 1, N, K, K)
+    q, qs = qvl.quantize_rows(dev(x, cuda), K)
+    c0 = np.random.default_rng(N).standard_normal((1, N), dtype=np.float32)
+    c = dev(c0.copy(), cuda)
+    qvl.linear_q16(q, qs, dev(w, cuda), dev(ws, cuda), K, C=c, semantics=qvl.SEM_LANE8 | qvl.SEM_ACCUMULATE)
+    want = (c0 + oracle.linear_i8(x, w, ws, K, oracle.LANE8)).astype(np.float32)
+    np.testing.assert_array_equal(c.cpu().numpy(), want)
+
+
 def test_swiglu_matches(qvl, cuda):
     rng = np.random.default_rng(4)
     g = (rng.standard_normal(6144, dtype=np.float32) * 4)
