@@ -279,6 +279,26 @@ def run_gemv(dev, steps=640, warmup=5):
             "launches_per_step": 2, "steps": steps}
 
 
+def run_gemv_line(args):
+    """BASELINE config 0 alone (one GPU): the INT8 GEMV 6144x2048 with
+    per-row scales, device-timed over rotated weight copies (> L2)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    with ClockSampler(0) as clk:
+        r = run_gemv(dev, steps=args.steps * 5, warmup=args.warmup)
+    peak, peak_kind = load_peaks()
+    print(json.dumps({
+        "metric": "int8_gemv_hbm_gbs", "value": r["kernel_gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps * 5, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic (seed 0, BASELINE config 0)",
+        "config": {"workload": WORKLOAD, "inputs": "64 rotated weight copies (805 MB > L2)"},
+        "roofline": {"bound": "hbm", "achieved": r["kernel_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": round(r["kernel_gbs"] / peak, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic("gemv_ring_config0"), "kernel": "gemv_ring_kernel"},
+        "step_with_quantisation_gbs": r["step_gbs"], "clocks": clk.summary()}))
+
+
 def decode_gemv_roofline(dec, steps=4):
     """Average GEMV launch of the decode step (q/k/v/o/gate/up/down x 28 +
     LM head), timed alone in a graph: algorithmic bytes / device time."""
@@ -632,7 +652,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_gemm"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_gemm", "gemv"])
     ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
                     help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")
     ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")
@@ -646,6 +666,8 @@ def main():
         run_prefill_gemm(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "gemv":
+        run_gemv_line(args)
     else:
         run_ours(args)
 
