@@ -279,6 +279,166 @@ def run_gemv(dev, steps=640, warmup=5):
             "launches_per_step": 2, "steps": steps}
 
 
+def ctypes_byref(x):
+    import ctypes
+    return ctypes.byref(x)
+
+
+def l2_flush_buffer(dev):
+    import torch
+    return torch.empty(256 << 20, dtype=torch.uint8, device=dev)    # 256 MB > the 126 MB L2
+
+
+def time_cold(fn, stream, flush, steps, warmup):
+    """Mean device time of fn() over `steps` launches, each preceded by an
+    untimed L2 flush (a 256 MB write), CUDA events on `stream`."""
+    import torch
+    torch.cuda.synchronize()          # inputs were initialised on the default stream
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+    return total / steps / 1e3
+
+
+def run_attention_line(args):
+    """GQA decode attention over FP16 KV pages (16 q / 8 kv
+    heads x 128), contexts {512, 4096, 32768} x decode batch {1, 8, 64}, one
+    query per request at the last position.  HBM-bound: 4096 bytes of K+V per
+    cached token per request.  L2 flushed before every timed launch."""
+    import torch
+    qvl = import_qvl()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = load_peaks()
+    stream = torch.cuda.Stream(dev)
+    flush = l2_flush_buffer(dev)
+    sweep = []
+    with ClockSampler(0) as clk:
+        for ctx in (512, 4096, 32768):
+            for B in (1, 8, 64):
+                kv = qvl.PagedKV(B, ctx, 16, 8, 128, 64, max_pos=ctx, device=dev)
+                kv.k.normal_()
+                kv.v.normal_()
+                q = torch.randn(B, 16, 128, device=dev)
+                out = torch.empty_like(q)
+                pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+                seq = torch.arange(B, dtype=torch.int32, device=dev)
+                work = qvl.Workspace(dev)
+                work.get(qvl.load_library().qvl_attention_workspace_bytes(B, ctx, ctypes_byref(kv.dims)))
+                fn = lambda: qvl.attention(q, kv, seq, pos, ctx, out=out, workspace=work)
+                sec = time_cold(fn, stream, flush, args.steps, args.warmup)
+                nbytes = 4096 * ctx * B + B * 16 * 128 * 4 * 2
+                sweep.append({"ctx": ctx, "batch": B, "us": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
+                              "frac": round(nbytes / sec / 1e9 / peak, 4)})
+                del kv, work
+                torch.cuda.empty_cache()
+    head = next(r for r in sweep if r["ctx"] == 32768 and r["batch"] == 64)
+    print(json.dumps({
+        "metric": "attention_decode_hbm_gbs", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 KV, fp32 softmax", "data": "synthetic N(0,1)",
+        "config": {"workload": "config3_gqa_decode_ctx32768_b64", "l2": "flushed before each launch"},
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": head["frac"], "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "attention (cluster kernel / split-K trio)"},
+        "sweep": sweep, "clocks": clk.summary()}))
+
+
+def int8_tensor_peak(dev):
+    """Measured int8 dense tensor throughput on this GPU (cuBLASLt through
+    torch._int_mm, 8192^3, best of 5), in TOPS (2*M*N*K)."""
+    import torch
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev).t()
+    try:
+        torch._int_mm(a, b)
+    except RuntimeError:
+        return None
+    torch.cuda.synchronize()
+    best = 0.0
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, 2 * n ** 3 / (e0.elapsed_time(e1) / 1e3) / 1e12)
+    return round(best, 1)
+
+
+def run_swiglu_line(args):
+    """the fused SwiGLU MLP down(silu(gate(x)) * up(x)),
+    int8 gate/up [6144,2048] and down [2048,6144] with per-row scales, M in
+    {1, 64, 512}; 8 rotated weight sets (302 MB > L2)."""
+    import torch
+    qvl = import_qvl()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = load_peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, I, NSET = 2048, 6144, 8
+    sets = []
+    for _ in range(NSET):
+        mk = lambda n, k: torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+        sc = lambda n: torch.rand(n, device=dev, generator=g) * 0.019 + 0.001
+        sets.append((mk(I, H), sc(I), mk(I, H), sc(I), mk(H, I), sc(H)))
+    i8peak = int8_tensor_peak(dev)
+    stream = torch.cuda.Stream(dev)
+    sweep = []
+    with ClockSampler(0) as clk:
+        for M in (1, 64, 512):
+            x = torch.randn(M, H, device=dev, generator=g)
+            out = torch.empty(M, H, device=dev)
+            work = qvl.Workspace(dev)
+            sem = qvl.SEM_REFERENCE
+            run = lambda i: qvl.swiglu_mlp(x, *sets[i % NSET], H, out=out, semantics=sem, workspace=work)
+            run(0)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(gr, stream=stream):
+                    for i in range(NSET):
+                        run(i)
+                for _ in range(args.warmup):
+                    gr.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(args.steps):
+                    gr.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+            sec = e0.elapsed_time(e1) / 1e3 / (args.steps * NSET)
+            nbytes = 3 * H * I + 4 * (2 * I + H) + 4 * M * H * 2
+            ops = 2 * M * 3 * H * I
+            r = {"M": M, "us": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
+                 "tops": round(ops / sec / 1e12, 2), "hbm_frac": round(nbytes / sec / 1e9 / peak, 4)}
+            if i8peak:
+                r["tensor_frac"] = round(ops / sec / 1e12 / i8peak, 4)
+            sweep.append(r)
+    head = sweep[0]
+    print(json.dumps({
+        "metric": "swiglu_mlp_hbm_gbs", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic (seed 0)",
+        "config": {"workload": "config2_swiglu_mlp_M1", "inputs": f"{NSET} rotated weight sets (302 MB > L2)"},
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": head["hbm_frac"], "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "gate/up GEMV (SwiGLU pair) + quantise + down GEMV"},
+        "int8_tensor_peak_tops": i8peak, "sweep": sweep, "clocks": clk.summary()}))
+
+
 def run_gemv_line(args):
     """BASELINE config 0 alone (one GPU): the INT8 GEMV 6144x2048 with
     per-row scales, device-timed over rotated weight copies (> L2)."""
@@ -400,6 +560,11 @@ def run_prefill_gemm(args):
     ops = sum(2 * M * N * K for N, K in PREFILL_SHAPES)
     tops = ops * args.steps * ws / (ms / 1e3) / 1e12
     if rank == 0:
+        i8peak = int8_tensor_peak(dev)
+        roofline_gemm = {"bound": "tensor", "achieved": round(tops / ws, 2), "peak": i8peak, "unit": "TOPS",
+                         "frac": round(tops / ws / i8peak, 4) if i8peak else None,
+                         "peak_kind": "measured (torch._int_mm int8, 8192^3, this GPU)", "traffic": None,
+                         "kernel": "gemm_i8_tc_kernel (tcgen05 kind::i8, hi/lo planes: 2 MMAs per algorithmic one)"}
         import oracle
         X, W, S, Y = mats[0]
         ref = oracle.linear_i8(X[:2].cpu().numpy(), W.cpu().numpy(), S.cpu().numpy(), 2048, oracle.TILED)
@@ -411,7 +576,7 @@ def run_prefill_gemm(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic",
             "config": {"workload": f"config1_gemm_M{M}", "shapes_NK": PREFILL_SHAPES,
                        "ops_per_step": ops, "note": "ops = 2*M*N*K (the hi/lo split doubles the MMA work)"},
-            "clocks": clk.summary(), "gpu_launches": 3 * len(PREFILL_SHAPES) * args.steps,
+            "roofline": roofline_gemm, "clocks": clk.summary(), "gpu_launches": 3 * len(PREFILL_SHAPES) * args.steps,
         }))
     if ws > 1:
         dist.destroy_process_group()
@@ -652,7 +817,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_gemm", "gemv"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "prefill_gemm", "gemv", "attention", "swiglu"])
     ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
                     help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")
     ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")
@@ -668,6 +834,10 @@ def main():
         run_prefill(args)
     elif args.workload == "gemv":
         run_gemv_line(args)
+    elif args.workload == "attention":
+        run_attention_line(args)
+    elif args.workload == "swiglu":
+        run_swiglu_line(args)
     else:
         run_ours(args)
 

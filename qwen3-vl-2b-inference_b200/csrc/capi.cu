@@ -355,7 +355,8 @@ int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
 
 size_t qvl_swiglu_mlp_workspace_bytes(size_t M, size_t H, size_t I, size_t g) {
     if (g == 0 || H % g || I % g) return 0;
-    return qbuf_bytes(M, H, g) + 2 * align256(M * I * sizeof(float)) + qbuf_bytes(M, I, g);
+    return qbuf_bytes(M, H, g) + 2 * align256(M * I * sizeof(float)) + qbuf_bytes(M, I, g) +
+           align256(qvl::gemm_tc_planes_bytes(M, H > I ? H : I));
 }
 
 int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const int8_t *Wu,
@@ -380,15 +381,17 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
     w += align256(M * I * 4);
     int16_t *qh = reinterpret_cast<int16_t *>(w);
     float *qhs = reinterpret_cast<float *>(w + align256(M * I * 2));
+    w += qbuf_bytes(M, I, group_size);
+    void *planes = w;        // hi/lo activation planes of the tensor-core path (M >= 16, TILED)
     cudaStream_t st = (cudaStream_t)stream;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)group_size, st));
     const bool l_gu = lane8_for(semantics, M, I, H);
-    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, group_size, l_gu, st);
-    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, group_size, l_gu, st);
+    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, group_size, l_gu, st, 0, planes);
+    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, group_size, l_gu, st, 0, planes);
     if (rc) return rc;
     QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)group_size, st));
     return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, group_size,
-                          lane8_for(semantics, M, H, I), st);
+                          lane8_for(semantics, M, H, I), st, 0, planes);
 }
 
 static int check_attn_dims(const qvl_attn_dims *d) {
