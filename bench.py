@@ -402,7 +402,8 @@ def run_swiglu_line(args):
             out = torch.empty(M, H, device=dev)
             work = qvl.Workspace(dev)
             sem = qvl.SEM_REFERENCE
-            run = lambda i: qvl.swiglu_mlp(x, *sets[i % NSET], H, out=out, semantics=sem, workspace=work)
+            # group_size 0: per-row scales for all three products (down: group 6144)
+            run = lambda i: qvl.swiglu_mlp(x, *sets[i % NSET], 0, out=out, semantics=sem, workspace=work)
             run(0)
             torch.cuda.synchronize()
             gr = torch.cuda.CUDAGraph()

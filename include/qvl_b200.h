@@ -168,6 +168,8 @@ int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, flo
 /* Fused MLP chain: out[M,H] = down(swiglu(gate(x), up(x))), the sequence of
  * model/src/forward.cpp:621-654 (gate/up linear, swiglu, down linear).
  * Wg, Wu: int8 [I, H]; Wd: int8 [H, I]; scales in the reference layout.
+ * group_size 0 = per-output-row scales for all three (gate/up [I], down [H]:
+ * the group is each product's K); otherwise one group size for all three.
  * Workspace: qvl_swiglu_mlp_workspace_bytes(M, H, I, group_size). */
 size_t qvl_swiglu_mlp_workspace_bytes(size_t M, size_t H, size_t I, size_t group_size);
 int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg,

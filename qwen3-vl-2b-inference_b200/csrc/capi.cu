@@ -354,8 +354,9 @@ int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
 }
 
 size_t qvl_swiglu_mlp_workspace_bytes(size_t M, size_t H, size_t I, size_t g) {
-    if (g == 0 || H % g || I % g) return 0;
-    return qbuf_bytes(M, H, g) + 2 * align256(M * I * sizeof(float)) + qbuf_bytes(M, I, g) +
+    const size_t g_in = g ? g : H, g_h = g ? g : I;     // 0: per-row, group = each product's K
+    if (H == 0 || I == 0 || H % g_in || I % g_h) return 0;
+    return qbuf_bytes(M, H, g_in) + 2 * align256(M * I * sizeof(float)) + qbuf_bytes(M, I, g_h) +
            align256(qvl::gemm_tc_planes_bytes(M, H > I ? H : I));
 }
 
@@ -365,8 +366,9 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
                       size_t workspace_bytes, void *stream) {
     if (!x || !Wg || !sg || !Wu || !su || !Wd || !sd || !out) return QVL_ERR_INVALID;
     if (!aligned(x, 16)) return QVL_ERR_INVALID;
-    int rc = check_linear_shape(M, I, H, group_size);
-    if (!rc) rc = check_linear_shape(M, H, I, group_size);
+    const size_t g_in = group_size ? group_size : H, g_h = group_size ? group_size : I;
+    int rc = check_linear_shape(M, I, H, g_in);
+    if (!rc) rc = check_linear_shape(M, H, I, g_h);
     if (rc) return rc;
     if (semantics < QVL_SEM_REFERENCE || semantics > QVL_SEM_TILED) return QVL_ERR_INVALID;
     const size_t need = qvl_swiglu_mlp_workspace_bytes(M, H, I, group_size);
@@ -374,23 +376,23 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
     char *w = static_cast<char *>(workspace);
     int16_t *qx = reinterpret_cast<int16_t *>(w);
     float *qxs = reinterpret_cast<float *>(w + align256(M * H * 2));
-    w += qbuf_bytes(M, H, group_size);
+    w += qbuf_bytes(M, H, g_in);
     float *gate = reinterpret_cast<float *>(w);
     w += align256(M * I * 4);
     float *up = reinterpret_cast<float *>(w);
     w += align256(M * I * 4);
     int16_t *qh = reinterpret_cast<int16_t *>(w);
     float *qhs = reinterpret_cast<float *>(w + align256(M * I * 2));
-    w += qbuf_bytes(M, I, group_size);
+    w += qbuf_bytes(M, I, g_h);
     void *planes = w;        // hi/lo activation planes of the tensor-core path (M >= 16, TILED)
     cudaStream_t st = (cudaStream_t)stream;
-    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)group_size, st));
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)g_in, st));
     const bool l_gu = lane8_for(semantics, M, I, H);
-    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, group_size, l_gu, st, 0, planes);
-    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, group_size, l_gu, st, 0, planes);
+    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, g_in, l_gu, st, 0, planes);
+    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, g_in, l_gu, st, 0, planes);
     if (rc) return rc;
-    QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)group_size, st));
-    return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, group_size,
+    QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)g_h, st));
+    return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, g_h,
                           lane8_for(semantics, M, H, I), st, 0, planes);
 }
 

@@ -119,6 +119,27 @@ def test_ring_gemv_accumulate(qvl, cuda, N, K):
     np.testing.assert_array_equal(c.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("M", [1, 64])
+def test_swiglu_mlp_per_row(qvl, cuda, M):
+    """group_size 0: per-row scales for gate/up (group 2048) and down (group
+    6144); M=64 runs the products on the tensor cores (TILED order)."""
+    H, I = 2048, 6144
+    rng = np.random.default_rng(70 + M)
+    x = rng.standard_normal((M, H), dtype=np.float32)
+    wg = rng.integers(-127, 128, (I, H), dtype=np.int8)
+    wu = rng.integers(-127, 128, (I, H), dtype=np.int8)
+    wd = rng.integers(-127, 128, (H, I), dtype=np.int8)
+    sg, su = (rng.uniform(0.001, 0.02, I).astype(np.float32) for _ in range(2))
+    sd = rng.uniform(0.001, 0.02, H).astype(np.float32)
+    out = qvl.swiglu_mlp(*(dev(a, cuda) for a in (x, wg, sg, wu, su, wd, sd)), group_size=0)
+    mode = oracle.LANE8_DISPATCH
+    h = oracle.swiglu(oracle.linear_i8(x, wg, sg, H, mode), oracle.linear_i8(x, wu, su, H, mode))
+    ref = oracle.linear_i8(h, wd, sd, I, mode)
+    got = out.cpu().numpy()
+    assert rel_err(got, ref) < REL_TOL_FP32
+    assert (got == ref).mean() > 0.99   # bit-exact except where expf rounding differs
+
+
 def test_swiglu_matches(qvl, cuda):
     rng = np.random.default_rng(4)
     g = (rng.standard_normal(6144, dtype=np.float32) * 4)
