@@ -391,7 +391,14 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
     rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, g_in, l_gu, st, 0, planes);
     if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, g_in, l_gu, st, 0, planes);
     if (rc) return rc;
-    QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)g_h, st));
+    if (g_h >= 4096) {
+        // whole-row groups: the SwiGLUs (double-precision exp) spread over the
+        // GPU in place in the gate scratch, then the row quantisation
+        QVL_CUDA_TRY(qvl::launch_swiglu(gate, up, (long)(M * I), st));
+        QVL_CUDA_TRY(qvl::launch_quantize_rows(gate, qh, qhs, (int)M, (int)I, (int)g_h, st));
+    } else {
+        QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)g_h, st));
+    }
     return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, g_h,
                           lane8_for(semantics, M, H, I), st, 0, planes);
 }
