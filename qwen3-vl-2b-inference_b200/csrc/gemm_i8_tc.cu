@@ -44,7 +44,7 @@ struct TcSmem {
     static constexpr int kBytes = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
 };
 
-// grid: (ceil(N/128), ceil(M/NT), SPLIT); block 128; with SPLIT > 1 the SPLIT
+// grid: (ceil(M/NT), ceil(N/128), SPLIT); block 128; with SPLIT > 1 the SPLIT
 // CTAs of a cluster (1, 1, SPLIT) each take K/SPLIT and their exact int32
 // partial sums are added through distributed shared memory (split-K keeps
 // small-N products -- decode batches -- spread over the GPU).
@@ -64,8 +64,10 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kBM;
-    const int m0 = blockIdx.y * NT;
+    // x = activation tile (fastest): the CTAs that share a weight tile run
+    // together, so the tile is read from HBM once and from L2 after
+    const int n0 = blockIdx.y * kBM;
+    const int m0 = blockIdx.x * NT;
     const int nk = K / kBK / SPLIT;             // stages of this CTA's K slice
     const int kb0 = blockIdx.z * nk;
     constexpr uint32_t kCols = (2 * NT < 32) ? 32 : 2 * NT;   // power of two >= 32
@@ -262,7 +264,7 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + kBM - 1) / kBM, (M + NT - 1) / NT, SPLIT);
+    cfg.gridDim = dim3((M + NT - 1) / NT, (N + kBM - 1) / kBM, SPLIT);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -281,7 +283,7 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
 }  // namespace
 
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
-    return M >= 16 && g == K && K % kBK == 0 && N >= kBM && get_encode() != nullptr;
+    return M >= 16 && g == K && K % kBK == 0 && N >= kBM && (N + kBM - 1) / kBM <= 65535 && get_encode() != nullptr;
 }
 
 size_t gemm_tc_planes_bytes(size_t M, size_t K) { return 2 * ((M * K + 255) & ~(size_t)255); }
