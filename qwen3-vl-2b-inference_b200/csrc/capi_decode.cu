@@ -14,7 +14,7 @@ struct DecodeWs {
 };
 constexpr DecodeWs decode_ws() {
     DecodeWs w{};
-    w.bar = 0;                                             // bar_count (u64), abort (int at +8)
+    w.bar = 0;                                             // bar_count (u64), abort (int at +8), head_bar [8] u64 at +64
     w.trace = 256;
     w.x_qkv = w.trace + qvl::kPersistTraceSlots * 8;
     w.h = w.x_qkv + al256((16 * 128 + 2 * 8 * 128) * 4);
@@ -111,6 +111,7 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
     ps.rope_sin = rope_sin;
     ps.max_ctx = max_ctx;
     ps.bar_count = reinterpret_cast<unsigned long long *>(ws);
+    ps.head_bar = reinterpret_cast<unsigned long long *>(ws + 64);
     ps.abort_flag = reinterpret_cast<int *>(ws + 8);
     ps.trace = reinterpret_cast<unsigned long long *>(ws + L.trace);
     QVL_CUDA_TRY(qvl::launch_decode_persistent(pw, ps, ctas, (cudaStream_t)stream));

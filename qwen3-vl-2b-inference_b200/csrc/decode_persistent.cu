@@ -86,6 +86,35 @@ __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
 // barrier (the CTA's writes are ordered by bar.sync, then published by the
 // release).  Returns false if the wait gave up or another CTA aborted.
 // CTA 0 records the time each barrier opens in S.trace[1 + k].
+// Barrier of the kSlices CTAs of one KV head (the softmax needs the maximum
+// over the head's slices only); same counter scheme as the grid barrier.
+__device__ __forceinline__ bool head_sync(const PersistState &S, int kvh) {
+    csync();
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        unsigned long long old, v;
+        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.head_bar + kvh) : "memory");
+        const unsigned long long target = (old / kSlices + 1) * kSlices;
+        int good = 1;
+        const unsigned long long t0 = global_ns();
+        for (unsigned it = 1;; ++it) {
+            asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.head_bar + kvh) : "memory");
+            if (v >= target) break;
+            if ((it & 15) == 0) {
+                if (ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag))) { good = 0; break; }
+                if (global_ns() - t0 > kBarrierLimitNs) {
+                    atomicExch(S.abort_flag, 1);
+                    good = 0;
+                    break;
+                }
+            }
+        }
+        ok = good;
+    }
+    csync();
+    return ok;
+}
+
 // Split into arrive and wait so that a CTA can load constants of the next
 // phase (norm weights, RoPE row) while the barrier completes.
 __device__ __forceinline__ void grid_arrive(const PersistState &S, unsigned long long &target) {
@@ -584,8 +613,8 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 1; w < kPWarps; ++w) m = fmaxf(m, redf[threadIdx.x][w]);
                 S.att_lmax[(kvh * 2 + threadIdx.x) * kSlices + sl] = m;
             }
+            if (!head_sync(S, kvh)) { drain(); return; }
         }
-        SYNC_OR_EXIT();
 
         // ---- attention, phase 2: probabilities (global max), slice sum, partial P.V
         if (attn_cta) {

@@ -40,6 +40,7 @@ struct PersistState {
     const float *rope_cos, *rope_sin;   // [max_pos, D/2]
     int max_ctx;
     unsigned long long *bar_count;      // grid barrier: arrivals since the workspace was zeroed
+    unsigned long long *head_bar;       // [NKV] barriers of the 16 slice CTAs of each KV head
     int *abort_flag;                    // set to 1 if a barrier wait timed out
     unsigned long long *trace;          // [kPersistTraceSlots] kernel start + barrier opening times (ns)
 };
