@@ -336,7 +336,7 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
 int *qvl_text_decode_abort_flag(void *workspace);
 /* Device address of the phase trace inside `workspace`: 256 uint64
  * global-timer stamps (ns) of the last call -- [0] kernel start, [1 + i] the
- * opening of grid barrier i (1 + 5 per layer + 1 barriers per token). */
+ * opening of grid barrier i (5 per layer + 1 barriers per token). */
 const uint64_t *qvl_text_decode_trace(const void *workspace);
 
 #ifdef __cplusplus

@@ -436,9 +436,10 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     // x (residual, written by other CTAs) -> RMSNorm with the staged weight
     // -> quantisation (one scale) into q16 / a_s_sh; arithmetic of
     // cta_norm_quant_row.
-    auto norm_quant_x = [&](bool inplace_form, int dbg = -1) {
-        for (int i = threadIdx.x; i < H / 4; i += kPThreads)
-            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.x) + i);
+    auto norm_quant_x = [&](bool inplace_form, int dbg = -1, bool x_in_smem = false) {
+        if (!x_in_smem)
+            for (int i = threadIdx.x; i < H / 4; i += kPThreads)
+                reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.x) + i);
         csync();
         if (dbg >= 0) DETAIL(dbg);
         if (threadIdx.x < 32) {
@@ -455,15 +456,19 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         if (dbg >= 0) DETAIL(dbg + 3);
     };
 
-    // embedding_lookup (per-row scale) of the input token into the residual stream
-    if (blockIdx.x == 0) {
+    // embedding_lookup (per-row scale) of the input token: every CTA forms
+    // the row in shared memory for the first RMSNorm (no barrier needed);
+    // CTA 0 also writes it to the residual stream, read after the next barrier
+    {
         const int id = (token >= 0 && token < W.vocab) ? token : 0;
         const float sc = W.embed_s[id];
-        for (int j = threadIdx.x; j < H; j += kPThreads) S.x[j] = mul_rn((float)W.embed[(size_t)id * H + j], sc);
+        for (int j = threadIdx.x; j < H; j += kPThreads) {
+            const float v = mul_rn((float)W.embed[(size_t)id * H + j], sc);
+            xs[j] = v;
+            if (blockIdx.x == 0) S.x[j] = v;
+        }
     }
-    GRID_ARRIVE();
     stage_norm(W.in_norm, W.in_norm_s);
-    GRID_WAIT_OR_EXIT();
 
     const int per = (ctx + kSlices - 1) / kSlices;
     const bool attn_cta = blockIdx.x < NKV * kSlices;
@@ -482,7 +487,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         // ---- input rms_norm + quantisation (every CTA), q/k/v blocks of the ring
-        norm_quant_x(false, l == 5 ? 240 : -1);
+        norm_quant_x(false, l == 5 ? 240 : -1, l == 0);
         if (l == 5) DETAIL(230);
         {
             const int nu = cta_units(ph_units(PH_QKV, W.vocab));
