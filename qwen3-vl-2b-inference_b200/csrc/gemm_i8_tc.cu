@@ -41,7 +41,10 @@ struct TcSmem {
     static constexpr int kA = kBM * kBK;          // 16 KB
     static constexpr int kB = NT * kBK;           // one activation plane
     static constexpr int kStage = kA + 2 * kB;
-    static constexpr int kBytes = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+    // 128-row activation tiles: 2 stages (96 KB), so two CTAs share an SM and
+    // one's epilogue overlaps the other's main loop; smaller tiles keep 4
+    static constexpr int kSt = NT >= 128 ? 2 : kStages;
+    static constexpr int kBytes = kSt * kStage + 1024 /* align */ + 256 /* barriers */;
 };
 
 // grid: (ceil(M/NT), ceil(N/128), SPLIT); block 128; with SPLIT > 1 the SPLIT
@@ -57,6 +60,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     using L = TcSmem<NT>;
+    constexpr int kStages = L::kSt;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * L::kStage);
     const uint32_t full0 = tc::smem_u32(bars);                 // [kStages]
     const uint32_t empty0 = tc::smem_u32(bars + kStages);      // [kStages]
