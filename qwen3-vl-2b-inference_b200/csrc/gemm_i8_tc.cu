@@ -43,7 +43,7 @@ struct TcSmem {
     static constexpr int kStage = kA + 2 * kB;
     // 128-row activation tiles: 2 stages (96 KB), so two CTAs share an SM and
     // one's epilogue overlaps the other's main loop; smaller tiles keep 4
-    static constexpr int kSt = NT >= 128 ? 2 : kStages;
+    static constexpr int kSt = NT >= 128 ? 2 : (NT >= 64 ? 3 : kStages);
     static constexpr int kBytes = kSt * kStage + 1024 /* align */ + 256 /* barriers */;
 };
 
