@@ -1,21 +1,26 @@
 """Benchmark of the B200 INT8 hot path (one JSON line on rank 0).
 
-Headline: decode tokens/s of the Qwen3-VL-2B text decoder (28 layers, int8
-per-row weights, tied 151936-row LM head) at batch 1 per GPU (``--batch``),
-after a 452-token prompt (196 vision + 256 text tokens; its KV state is
-synthetic), one step = one generated token per request, 128 steps by default.
-The config-0 GEMV (below) is reported as ``gemv_config0``.
+Headline (BASELINE metric "decode tokens/s (batch 1/32)"): decode tokens/s of
+the Qwen3-VL-2B text decoder -- 28 layers, int8 per-row weights, tied
+151936-row LM head, random-init (no checkpoint) -- at ``--batch`` requests
+per GPU (default 1), after a 452-position prompt state (196 vision + 256 text
+positions of BASELINE config 4; the KV contents are synthetic).  One step =
+one generated token per request.  At batch 1 a step is ONE cooperative
+launch (decode_persistent_kernel), captured in a CUDA graph; attention runs in
+the reference's summation order by default (``--attn-order``), so the logits
+are bit-identical to the reference's operators.  The same line carries
+``batch32`` (32 requests on the tensor cores), ``gemv_config0`` (BASELINE
+config 0, the INT8 GEMV alone), ``e2e`` (token ids through pinned host memory
+every step), ``roofline`` and ``cpu_baseline``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|gemv|prefill|prefill_gemm|swiglu|attention]
 
-Workload: x fp32 [1,2048] ~N(0,1), W int8 [6144,2048]
-~U[-127,127], per-output-row fp32 scales ~U(0.001,0.02), seed 0;
-y = x (W*s)^T.  One step = activation quantisation + INT8 GEMV.  64 distinct
-weight copies (805 MB, > 6x the 126 MB L2) are rotated so every step streams
-its weights from HBM.  Under torchrun every rank runs its own replica (the
-path has no exchange step), so scaling is weak and the job value is the sum.
+Under torchrun every rank runs its own replica (decode requests are
+independent; no collective on the data path), so scaling is weak and the job
+value is the sum over ranks; time is the max over ranks.
 
-``--impl reference`` times the reference engine's own CPU kernel
+``--impl reference`` times the reference engine's own CPU operators
 (oracle/_ref, compiled from its sources) on this host's cores, same metric.
 """
 from __future__ import annotations
@@ -647,6 +652,44 @@ def run_prefill(args):
         dist.destroy_process_group()
 
 
+def run_decode_batch(w, B, args, dev):
+    """Decode tokens/s at B requests on this GPU (tensor-core products in the
+    reference's M>1 order, one graph-captured step per token), for the
+    "batch 32" half of the headline metric."""
+    import torch
+    import qvl_b200.decoder as D
+    steps = args.batch32_steps
+    max_ctx = PROMPT_CTX + args.warmup + steps + 8
+    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev, attn_order=args.attn_order)
+    D.fill_kv_random(dec, PROMPT_CTX, seed=B)
+    dec.tokens.copy_(torch.arange(B, dtype=torch.int32, device=dev) * 7919 % dec.cfg.vocab)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        dec.step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dec.step()
+        dec.positions.fill_(PROMPT_CTX)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    w_bytes = sum(v.numel() * v.element_size() for v in w.t.values())
+    out = {"tokens_per_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4), "batch": B, "steps": steps,
+           "order": "tiled (M=32 tcgen05 products, reference M>1 order)" if dec.use_tc else "lane8",
+           "step_hbm_gbs": round(w_bytes / (ms / 1e3) / 1e9, 1)}
+    del dec, g
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -662,7 +705,8 @@ def run_ours(args):
     max_ctx = PROMPT_CTX + args.warmup + args.steps + 8
     w = D.TextWeights.random(cfg, seed=rank, device=dev)
     persistent = args.engine == "persistent" or (args.engine == "auto" and B == 1 and max_ctx <= 8192)
-    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev, persistent=persistent)
+    dec = D.TextDecoder(w, max_batch=B, max_ctx=max_ctx, device=dev, persistent=persistent,
+                        attn_order=args.attn_order)
     D.fill_kv_random(dec, PROMPT_CTX, seed=rank)
     dec.tokens.copy_(torch.arange(B, dtype=torch.int32, device=dev) * 7919 % cfg.vocab)
     stream = torch.cuda.Stream(dev)
@@ -743,11 +787,13 @@ def run_ours(args):
     lib = qvl.load_library()
     tc_mode = dec.use_tc
     attn_k = 1 if max_ctx <= 8192 else 3          # cluster kernel / split-K trio
+    if args.attn_order == "reference":
+        attn_k = 2                                  # ordered scores + softmax/P.V
     if dec.use_tc:   # rmsnorm, split+3 GEMMs, rope, attention, quantize, split+GEMM, rmsnorm,
         # split+2 GEMMs+swiglu, quantize, split+GEMM
         per_layer, head = 1 + 4 + 1 + attn_k + 1 + 2 + 1 + 4 + 1 + 2, 1 + 1 + 2 + 1
     elif B == 1:  # qkv, rope, attention(+quantise tail), o(+norm tail), gate/up(+quant tail), down(+norm tail)
-        per_layer, head = 5 + (1 if attn_k == 1 else 4), 1 + 1 + 1 + 1  # embedding, first rmsnorm, LM head, argmax
+        per_layer, head = 5 + (1 if attn_k == 1 else attn_k + 1), 1 + 1 + 1 + 1  # embedding, first rmsnorm, LM head, argmax
     elif B <= 4:  # fast GEMV without the fused tails
         per_layer, head = 9 + attn_k, 1 + 2 + 1
     else:        # 8-row GEMV tiles, separate norms / swiglu
@@ -759,6 +805,10 @@ def run_ours(args):
         aborted = qvl.text_decode_aborted(dec.pws)
         if aborted:
             raise RuntimeError("persistent decode: a grid barrier wait timed out")
+    batch32 = None
+    if rank == 0 and args.batch == 1 and args.batch32_steps > 0:
+        del g, ge
+        batch32 = run_decode_batch(w, 32, args, dev)
     gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = load_peaks()
@@ -780,7 +830,7 @@ def run_ours(args):
             roofline = gemv_roof
         cpu = None
         if args.cpu_seconds > 0:
-            del dec, g, ge
+            del dec
             torch.cuda.empty_cache()
             tps, n, dt = cpu_decode_rate(args, seconds=args.cpu_seconds)
             import oracle
@@ -795,6 +845,9 @@ def run_ours(args):
             "dtype": "int16xint8->int32", "data": "synthetic (random-init int8 weights, seed = rank)",
             "config": dict(decode_config(args, ws),
                            engine="persistent (one launch per token)" if persistent else "launch chain",
+                           attn_order=("reference (the reference's summation order: logits bit-identical "
+                                       "to its operators)") if args.attn_order == "reference"
+                           else "fast (context split over CTAs)",
                            batch_order="tiled (M=B tcgen05, reference M>1 order)" if tc_mode
                            else "lane8 (each request in the reference M=1 order)"),
             "roofline": roofline,
@@ -805,6 +858,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "gemv_config0": gemv0,
+            "batch32": batch32,
         }))
     if ws > 1:
         dist.destroy_process_group()
@@ -820,6 +874,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "prefill_gemm", "gemv", "attention", "swiglu"])
+    ap.add_argument("--attn-order", default="reference", choices=["reference", "fast"],
+                    help="decode attention: the reference's summation order (bit-identical logits) or split context")
+    ap.add_argument("--batch32-steps", type=int, default=32, help="steps of the batch-32 figure (0: skip)")
     ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
                     help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")
     ap.add_argument("--m", type=int, default=512, help="prefill_gemm: activation rows")

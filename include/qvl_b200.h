@@ -63,6 +63,15 @@ extern "C" {
 #define QVL_SEM_TILED 2
 
 const char *qvl_status_string(int status);
+/* Tensor-core timeout word of the current device.  The tensor-core path
+ * (M >= 16 products) bounds every wait; a wait that gives up sets the word,
+ * and while it is set every tensor-core launch on that device leaves without
+ * computing.  Launches are asynchronous, so the call that timed out still
+ * returned QVL_OK: this synchronises `stream`, stores 1 in *timed_out if the
+ * word is set (the outputs since it was last cleared are invalid) and, with
+ * `clear`, resets it so that the path computes again.  No counterpart in the
+ * reference (its operators are synchronous and cannot time out). */
+int qvl_tc_timeout_status(int *timed_out, int clear, void *stream);
 /* Last CUDA error code recorded by a QVL_ERR_CUDA return (0 if none). */
 int qvl_last_cuda_error(void);
 /* Library version, e.g. "qvl_b200 0.1". */
@@ -216,6 +225,23 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
                          const qvl_attn_dims *dims, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* qvl_attention_decode in the reference's own summation order, bit for bit
+ * given the same fp16-valued cache: each score in the order of
+ * attn_scores_all_heads (the 8-position unrolled loop and its 0-7 tail,
+ * layers/src/text_layer.cpp:575-650), softmax's 8 float lanes plus double
+ * tail (:436-535), and one fma chain over t ascending per output element
+ * (attn_weighted_sum_all_heads, :655-710).  The chains run sequentially, so
+ * this is slower than qvl_attention_decode at long contexts; it is the
+ * attention of the decoder's reference-order mode.  workspace:
+ * qvl_attention_ordered_workspace_bytes(nq, max_ctx, dims) bytes (scores,
+ * 256-byte aligned); nq <= 65535. */
+size_t qvl_attention_ordered_workspace_bytes(size_t nq, int max_ctx, const qvl_attn_dims *dims);
+int qvl_attention_decode_ordered(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                                 const int32_t *page_table, const int32_t *seq_ids,
+                                 const int32_t *positions, size_t nq, int max_ctx, float *out,
+                                 const qvl_attn_dims *dims, void *workspace,
+                                 size_t workspace_bytes, void *stream);
+
 /* qvl_attention_decode followed by the activation quantisation of each
  * output row (one scale per row, the o_proj input): q_out int16 [nq, NH*D],
  * q_out_scales fp32 [nq].  Fused into the attention launch when it runs as
@@ -299,7 +325,10 @@ int qvl_argmax_rows(const float *logits, int32_t *idx, size_t rows, size_t n, vo
  * One cooperative kernel: every CTA stays resident for the whole token and
  * the phases meet at a grid barrier whose waits are bounded (2 s); a timeout
  * sets an abort word in the workspace (qvl_text_decode_abort_flag) and every
- * CTA leaves.  Arithmetic per operation is that of the separate entry points
+ * CTA leaves.  A call whose *pos is outside [0, max_ctx) or whose *token is
+ * outside [0, vocab) decodes nothing: it sets the abort word to 2 (position)
+ * or 3 (token) and leaves token, pos, x, logits and the KV cache unchanged.
+ * rope_cos / rope_sin need max_ctx rows.  Arithmetic per operation is that of the separate entry points
  * with QVL_SEM_LANE8 (M=1 GEMV order); the attention splits each context into
  * 16 slices, so its fp32 partial sums are grouped differently.
  *
@@ -332,7 +361,20 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
                          const int32_t *page_table, int page_size, const float *rope_cos,
                          const float *rope_sin, int max_ctx, void *workspace,
                          size_t workspace_bytes, void *stream);
-/* Device address of the abort word inside `workspace` (int, 0 = healthy). */
+/* qvl_text_decode_step with flags.  QVL_DECODE_REFERENCE_ORDER: attention in
+ * the reference's own summation order (see qvl_attention_decode_ordered), so
+ * that the whole token -- logits and greedy id -- is bit-identical to the
+ * reference's operators on the same fp16-valued cache; the softmax sum and
+ * the P.V chains then run sequentially over the context in one CTA per KV
+ * head, which costs a few microseconds per layer. */
+#define QVL_DECODE_REFERENCE_ORDER 1
+int qvl_text_decode_step_ex(const qvl_text_weights *w, float *x, float *logits, int32_t *token,
+                            int32_t *pos, uint16_t *k_pages, uint16_t *v_pages, long kv_layer_stride,
+                            const int32_t *page_table, int page_size, const float *rope_cos,
+                            const float *rope_sin, int max_ctx, void *workspace,
+                            size_t workspace_bytes, int flags, void *stream);
+/* Device address of the abort word inside `workspace` (int): 0 healthy, 1 a
+ * bounded wait gave up, 2 position out of range, 3 token out of range. */
 int *qvl_text_decode_abort_flag(void *workspace);
 /* Device address of the phase trace inside `workspace`: 256 uint64
  * global-timer stamps (ns) of the last call -- [0] kernel start, [1 + i] the

@@ -20,7 +20,24 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libqwen_ref.so")
-REF_SRC = os.environ.get("QVL_REFERENCE_DIR", "/root/reference")
+
+
+def _reference_dir():
+    """Where the reference sources are: $QVL_REFERENCE_DIR, else the
+    `reference_path` that BASELINE.json at the repository root names (absent
+    on machines without the sources; the built library then travels)."""
+    d = os.environ.get("QVL_REFERENCE_DIR")
+    if d:
+        return d
+    try:
+        import json
+        with open(os.path.join(HERE, "..", "BASELINE.json")) as f:
+            return json.load(f).get("reference_path") or ""
+    except (OSError, ValueError):
+        return ""
+
+
+REF_SRC = _reference_dir()
 
 LANE8_DISPATCH, LANE8, TILED = 0, 1, 2
 
@@ -32,7 +49,7 @@ _I = ctypes.c_int
 def build(ref: bool = True) -> None:
     """Compile the restatement, and the reference library when its sources exist."""
     subprocess.run(["make", "-C", HERE, "-s", "all"], check=True)
-    if ref and os.path.isdir(REF_SRC):
+    if ref and REF_SRC and os.path.isdir(REF_SRC):
         subprocess.run(["make", "-C", HERE, "-s", "-j8", "ref", f"REF={REF_SRC}"], check=True)
 
 
@@ -55,6 +72,7 @@ def lib():
         L.orc_linear_i8.argtypes = [_P, _P, _P, _P, _Z, _Z, _Z, _Z, _I]
         L.orc_group_sums.argtypes = [_P, _P, _P, _Z, _Z, _Z, _Z]
         L.orc_swiglu.argtypes = [_P, _P, _Z]
+        L.orc_expf.argtypes = [_P, _P, _Z]
         L.orc_exp_ref.argtypes = [ctypes.c_float]
         L.orc_exp_ref.restype = ctypes.c_float
         L.orc_softmax.argtypes = [_P, _Z]
@@ -102,11 +120,25 @@ def quantize(x: np.ndarray, g: int):
     return q, s
 
 
-def linear_i8(x, w, ws, g, mode=LANE8_DISPATCH):
+def linear_i8(x, w, ws, g, mode=LANE8_DISPATCH, threads=1):
+    """y = x . dequant(w)^T in the reference's order.  With an explicit mode
+    (LANE8 or TILED) every output row depends on its own input row only, so
+    `threads` > 1 splits the rows over host threads (ctypes drops the GIL)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M, K = x.shape
     N = w.shape[0]
     y = np.empty((M, N), np.float32)
+    if threads > 1 and mode != LANE8_DISPATCH and M > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        bounds = np.linspace(0, M, min(threads, M) + 1).astype(int)
+
+        def part(i):
+            a, b = bounds[i], bounds[i + 1]
+            if b > a:
+                lib().orc_linear_i8(x[a:b].ctypes.data, _ptr(w), _ptr(ws), y[a:b].ctypes.data, b - a, N, K, g, mode)
+        with ThreadPoolExecutor(len(bounds) - 1) as ex:
+            list(ex.map(part, range(len(bounds) - 1)))
+        return y
     lib().orc_linear_i8(_ptr(x), _ptr(w), _ptr(ws), _ptr(y), M, N, K, g, mode)
     return y
 
@@ -124,6 +156,21 @@ def swiglu(gate, up):
     u = np.ascontiguousarray(up, dtype=np.float32)
     lib().orc_swiglu(_ptr(g), _ptr(u), g.size)
     return g
+
+
+def expf(x, threads=1):
+    """The host C library's expf, elementwise (rows split over threads)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    y = np.empty_like(x)
+    if threads <= 1:
+        lib().orc_expf(_ptr(x), _ptr(y), x.size)
+        return y
+    from concurrent.futures import ThreadPoolExecutor
+    b = np.linspace(0, x.size, threads + 1).astype(np.int64)
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda i: lib().orc_expf(x[b[i]:].ctypes.data, y[b[i]:].ctypes.data, int(b[i + 1] - b[i])),
+                    range(threads)))
+    return y
 
 
 def softmax(x):

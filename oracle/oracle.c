@@ -128,6 +128,13 @@ void orc_swiglu(float *gate, const float *up, size_t n) {
     }
 }
 
+/* The host C library's expf, elementwise over a buffer: what the reference's
+ * swiglu calls (layers/src/text_layer.cpp:430, scalar expf; the object file
+ * of text_layer.cpp references the libm symbol expf). */
+void orc_expf(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
+}
+
 /* exp256_ps, layers/include/simd_utils.hpp:7-47, one lane: clamp to
  * +-88.3762626647949, n = floor(x*log2e), g = x - n*ln2 (fused),
  * y = 1 + g + g^2/2 + g^3/6 + g^4/24 (Horner-free, fused adds),
@@ -214,12 +221,27 @@ void orc_attention(const float *key_cache, const float *value_cache, const float
         const float *qh = q + (size_t)h * D;
         const float *kh = key_cache + (size_t)(h / kv_mul) * S * D;
         float *ah = att + (size_t)h * S;
+        /* positions [0, 8*(pos/8)): the 8-position unrolled loop (:590-633),
+         * 8 fused lanes then add_reduce_mm_256_layer; the 0-7 tail (:636-645):
+         * `#pragma omp simd reduction(+:score)` over `score += q*k`, which g++
+         * (-std=c++17 -O3 -fopenmp -mavx2 -mfma, no FP contraction in ISO
+         * mode) vectorises as 8 lanes of unfused multiply-adds whose partial
+         * sums are then added lane 0..7 in order onto the initial 0. */
+        const int tail0 = (pos / 8) * 8;
         for (int t = 0; t <= pos; ++t) {
             float l8[8] = {0};
             const float *kt = kh + (size_t)t * D;
-            for (int i = 0; i < D; i += 8)
-                for (int l = 0; l < 8; ++l) l8[l] = fmaf(qh[i + l], kt[i + l], l8[l]);
-            ah[t] = reduce8(l8) * inv_sqrt_d;
+            if (t < tail0) {
+                for (int i = 0; i < D; i += 8)
+                    for (int l = 0; l < 8; ++l) l8[l] = fmaf(qh[i + l], kt[i + l], l8[l]);
+                ah[t] = reduce8(l8) * inv_sqrt_d;
+            } else {
+                for (int i = 0; i < D; i += 8)
+                    for (int l = 0; l < 8; ++l) l8[l] = l8[l] + qh[i + l] * kt[i + l];
+                float r = l8[0];
+                for (int l = 1; l < 8; ++l) r = r + l8[l];
+                ah[t] = (0.0f + r) * inv_sqrt_d;
+            }
         }
         orc_softmax(ah, (size_t)pos + 1);
     }

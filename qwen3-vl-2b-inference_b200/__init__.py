@@ -47,7 +47,9 @@ EXPORTED = (
     "qvl_swiglu_quantize_rows", "qvl_linear_q16_i8_multi", "qvl_gate_up_swiglu_q16_i8",
     "qvl_linear_q16_i8_tail", "qvl_linear_q16_i8_batched", "qvl_linear_q16_i8_batched_workspace_bytes",
     "qvl_attention_decode_q16", "qvl_text_decode_workspace_bytes", "qvl_text_decode_step",
-    "qvl_text_decode_abort_flag", "qvl_text_decode_trace",
+    "qvl_text_decode_step_ex",
+    "qvl_text_decode_abort_flag", "qvl_text_decode_trace", "qvl_tc_timeout_status",
+    "qvl_attention_decode_static", "qvl_attention_ordered_workspace_bytes", "qvl_attention_decode_ordered",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -108,6 +110,9 @@ def load_library(path: str = LIB_PATH):
     L.qvl_attention_workspace_bytes.restype = _Z
     L.qvl_attention_workspace_bytes.argtypes = [_Z, _I, ctypes.POINTER(AttnDims)]
     L.qvl_attention_decode.argtypes = [_P] * 6 + [_Z, _I, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
+    L.qvl_attention_ordered_workspace_bytes.restype = _Z
+    L.qvl_attention_ordered_workspace_bytes.argtypes = [_Z, _I, ctypes.POINTER(AttnDims)]
+    L.qvl_attention_decode_ordered.argtypes = [_P] * 6 + [_Z, _I, _P, ctypes.POINTER(AttnDims), _P, _Z, _P]
     L.qvl_argmax_rows.argtypes = [_P, _P, _Z, _Z, _P]
     L.qvl_qknorm_rope_kv_append.argtypes = [_P] * 8 + [_Z, _P, _P, _P, _P, _P, _P, _Z, ctypes.c_float,
                                                        ctypes.POINTER(AttnDims), _P]
@@ -126,10 +131,13 @@ def load_library(path: str = LIB_PATH):
     L.qvl_text_decode_workspace_bytes.argtypes = []
     L.qvl_text_decode_step.argtypes = [ctypes.POINTER(TextWeightsC)] + [_P] * 6 + [ctypes.c_long, _P, _I, _P, _P,
                                                                                 _I, _P, _Z, _P]
+    L.qvl_text_decode_step_ex.argtypes = L.qvl_text_decode_step.argtypes[:-1] + [_I, _P]
     L.qvl_text_decode_abort_flag.restype = _P
     L.qvl_text_decode_abort_flag.argtypes = [_P]
     L.qvl_text_decode_trace.restype = _P
     L.qvl_text_decode_trace.argtypes = [_P]
+    L.qvl_tc_timeout_status.argtypes = [ctypes.POINTER(_I), _I, _P]
+    L.qvl_internal_set_tc_timeout.argtypes = [_P]
     _lib = L
     return L
 
@@ -292,6 +300,22 @@ def attention(q, kv: PagedKV, seq_ids, positions, max_ctx, out=None, workspace=N
     return out
 
 
+def attention_ordered(q, kv: PagedKV, seq_ids, positions, max_ctx, out=None, workspace=None, stream=None):
+    """attention() in the reference's own summation order (bit-exact with
+    attn_scores_all_heads + softmax + attn_weighted_sum_all_heads on the same
+    fp16-valued cache); sequential over the context, so slower."""
+    nq = q.shape[0]
+    if out is None:
+        out = torch.empty_like(q)
+    L = load_library()
+    ws = _ws(workspace, q.device).get(L.qvl_attention_ordered_workspace_bytes(nq, max_ctx, ctypes.byref(kv.dims)))
+    _check(L.qvl_attention_decode_ordered(_ptr(q), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table),
+                                          _ptr(seq_ids), _ptr(positions), nq, max_ctx, _ptr(out),
+                                          ctypes.byref(kv.dims), _ptr(ws), ws.numel(), _stream(stream)),
+           "attention_ordered")
+    return out
+
+
 def text_weights_struct(t: dict, cfg) -> TextWeightsC:
     """qvl_text_weights for the stacked weight dict of decoder.TextWeights
     (the tensors must stay alive while the struct is used)."""
@@ -315,16 +339,28 @@ def text_decode_workspace(device) -> torch.Tensor:
     return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
+DECODE_REFERENCE_ORDER = 1
+
+
 def text_decode_step(w: TextWeightsC, x, logits, token, pos, k_all, v_all, page_table, page_size, rope_cos,
-                     rope_sin, max_ctx, workspace, stream=None):
+                     rope_sin, max_ctx, workspace, stream=None, flags=0):
     """One whole decode token of one request in one launch: reads token[0] and
     pos[0], writes logits and x, replaces token[0] by the greedy token and
-    advances pos[0].  k_all / v_all: [layers, pages, NKV, page_size, D] fp16."""
+    advances pos[0].  k_all / v_all: [layers, pages, NKV, page_size, D] fp16.
+    flags=DECODE_REFERENCE_ORDER: attention in the reference's summation order."""
     layer_stride = k_all[0].numel()
-    _check(load_library().qvl_text_decode_step(
+    _check(load_library().qvl_text_decode_step_ex(
         ctypes.byref(w), _ptr(x), _ptr(logits), _ptr(token), _ptr(pos), _ptr(k_all), _ptr(v_all), layer_stride,
         _ptr(page_table), page_size, _ptr(rope_cos), _ptr(rope_sin), max_ctx, _ptr(workspace),
-        workspace.numel(), _stream(stream)), "text_decode_step")
+        workspace.numel(), flags, _stream(stream)), "text_decode_step")
+
+
+def tc_timed_out(clear: bool = False, stream=None) -> bool:
+    """True if a bounded wait of the tensor-core GEMM gave up on this device
+    since the word was last cleared (synchronises); clear=True resets it."""
+    v = _I(0)
+    _check(load_library().qvl_tc_timeout_status(ctypes.byref(v), int(clear), _stream(stream)), "tc_timeout_status")
+    return bool(v.value)
 
 
 def text_decode_aborted(workspace) -> bool:

@@ -54,7 +54,7 @@ extern "C" int qvl_attention_decode_static(const float *q, const uint16_t *k_pag
     void *scratch = nullptr;
     int rc = scratch_for_current_device(&scratch);
     if (rc) return rc;
-    qvl::AttnArgs a;
+    qvl::AttnArgs a = {};
     a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
     a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
     a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;

@@ -10,6 +10,7 @@
 #include "gemm_i8_tc.cuh"
 #include "gemv_ring.cuh"
 #include "swiglu.cuh"
+#include "attention_ordered.cuh"
 #include "attention.cuh"
 #include "argmax.cuh"
 #include "norm.cuh"
@@ -118,6 +119,31 @@ const char *qvl_status_string(int s) {
 int qvl_last_cuda_error(void) { return g_last_cuda_error; }
 
 const char *qvl_version(void) { return "qvl_b200 0.1"; }
+
+int qvl_tc_timeout_status(int *timed_out, int clear, void *stream) {
+    if (!timed_out) return QVL_ERR_INVALID;
+    int *word = qvl::gemm_tc_timeout_word();
+    if (!word) return QVL_ERR_CUDA;
+    cudaStream_t st = (cudaStream_t)stream;
+    int v = 0;
+    QVL_CUDA_TRY(cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, st));
+    QVL_CUDA_TRY(cudaStreamSynchronize(st));
+    *timed_out = v != 0;
+    if (clear && v) {
+        QVL_CUDA_TRY(cudaMemsetAsync(word, 0, sizeof(int), st));
+        QVL_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return QVL_OK;
+}
+
+int qvl_internal_set_tc_timeout(void *stream) {
+    int *word = qvl::gemm_tc_timeout_word();
+    if (!word) return QVL_ERR_CUDA;
+    const int one = 1;
+    QVL_CUDA_TRY(cudaMemcpyAsync(word, &one, sizeof(int), cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    QVL_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+    return QVL_OK;
+}
 
 int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, size_t K,
                       size_t group_size, void *stream) {
@@ -346,6 +372,14 @@ int qvl_linear_q16_i8_batched(const int16_t *q, const float *q_scales, size_t n_
     return QVL_OK;
 }
 
+// Test hook: the expf the SwiGLU kernels use, elementwise (not in the header).
+int qvl_internal_expf(const float *x, float *y, size_t n, void *stream) {
+    if (!x || !y) return QVL_ERR_INVALID;
+    if (n == 0) return QVL_OK;
+    QVL_CUDA_TRY(qvl::launch_expf_host(x, y, (long)n, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
 int qvl_swiglu(float *gate, const float *up, size_t n, void *stream) {
     if (!gate || !up) return QVL_ERR_INVALID;
     if (n == 0) return QVL_OK;
@@ -516,6 +550,33 @@ int qvl_attention_decode(const float *q, const uint16_t *k_pages, const uint16_t
     a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
     a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
     QVL_CUDA_TRY(qvl::launch_attention(a, workspace, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+size_t qvl_attention_ordered_workspace_bytes(size_t nq, int max_ctx, const qvl_attn_dims *dims) {
+    if (check_attn_dims(dims) || max_ctx <= 0) return 0;
+    return qvl::attn_ordered_workspace_bytes(nq, max_ctx, dims->num_heads);
+}
+
+int qvl_attention_decode_ordered(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                                 const int32_t *page_table, const int32_t *seq_ids, const int32_t *positions,
+                                 size_t nq, int max_ctx, float *out, const qvl_attn_dims *dims, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !k_pages || !v_pages || !page_table || !seq_ids || !positions || !out) return QVL_ERR_INVALID;
+    if (max_ctx <= 0) return QVL_ERR_INVALID;
+    if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(q, 16)) return QVL_ERR_INVALID;
+    if (nq == 0) return QVL_OK;
+    if (nq > 65535) return QVL_ERR_UNSUPPORTED;
+    const size_t need = qvl::attn_ordered_workspace_bytes(nq, max_ctx, dims->num_heads);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    qvl::AttnArgs a = {};
+    a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
+    a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    QVL_CUDA_TRY(qvl::launch_attention_ordered(a, workspace, (cudaStream_t)stream));
     return QVL_OK;
 }
 

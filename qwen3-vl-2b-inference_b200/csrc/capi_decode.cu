@@ -10,7 +10,7 @@ constexpr size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 // Workspace layout; the barrier words come first so that they keep their
 // place whatever the device's SM count.
 struct DecodeWs {
-    size_t bar, trace, x_qkv, h, lmax, lsum, pacc, cnt, att, best_v, best_i, total;
+    size_t bar, trace, x_qkv, h, lmax, lsum, pacc, cnt, att, best_v, best_i, e, total;
 };
 constexpr DecodeWs decode_ws() {
     DecodeWs w{};
@@ -25,7 +25,8 @@ constexpr DecodeWs decode_ws() {
     w.att = w.cnt + 256;
     w.best_v = w.att + al256(16 * 128 * 4);
     w.best_i = w.best_v + al256(kMaxCtas * qvl::kPersistWarpsPerCta * 4);
-    w.total = w.best_i + al256(kMaxCtas * qvl::kPersistWarpsPerCta * 4);
+    w.e = w.best_i + al256(kMaxCtas * qvl::kPersistWarpsPerCta * 4);
+    w.total = w.e + al256(16 * qvl::kPersistSlices * 512 * 4);
     return w;
 }
 
@@ -49,6 +50,15 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
                          uint16_t *k_pages, uint16_t *v_pages, long kv_layer_stride, const int32_t *page_table,
                          int page_size, const float *rope_cos, const float *rope_sin, int max_ctx, void *workspace,
                          size_t workspace_bytes, void *stream) {
+    return qvl_text_decode_step_ex(w, x, logits, token, pos, k_pages, v_pages, kv_layer_stride, page_table,
+                                   page_size, rope_cos, rope_sin, max_ctx, workspace, workspace_bytes, 0, stream);
+}
+
+int qvl_text_decode_step_ex(const qvl_text_weights *w, float *x, float *logits, int32_t *token, int32_t *pos,
+                            uint16_t *k_pages, uint16_t *v_pages, long kv_layer_stride, const int32_t *page_table,
+                            int page_size, const float *rope_cos, const float *rope_sin, int max_ctx,
+                            void *workspace, size_t workspace_bytes, int flags, void *stream) {
+    if (flags & ~QVL_DECODE_REFERENCE_ORDER) return QVL_ERR_INVALID;
     if (!w || !x || !logits || !token || !pos || !k_pages || !v_pages || !page_table || !rope_cos || !rope_sin)
         return QVL_ERR_INVALID;
     const void *ptrs[] = {w->w_q, w->w_k, w->w_v, w->w_o, w->w_gate, w->w_up, w->w_down, w->s_q, w->s_k,
@@ -96,6 +106,8 @@ int qvl_text_decode_step(const qvl_text_weights *w, float *x, float *logits, int
     ps.att_lmax = reinterpret_cast<float *>(ws + L.lmax);
     ps.att_lsum = reinterpret_cast<double *>(ws + L.lsum);
     ps.att_pacc = reinterpret_cast<float *>(ws + L.pacc);
+    ps.att_e = reinterpret_cast<float *>(ws + L.e);
+    ps.ordered = (flags & QVL_DECODE_REFERENCE_ORDER) ? 1 : 0;
     ps.att_cnt = reinterpret_cast<int *>(ws + L.cnt);
     ps.att_out = reinterpret_cast<float *>(ws + L.att);
     ps.warp_best_v = reinterpret_cast<float *>(ws + L.best_v);

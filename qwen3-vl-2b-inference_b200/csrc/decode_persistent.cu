@@ -361,6 +361,15 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         if (blockIdx.x == 0) S.trace[0] = global_ns();
         // a workspace left aborted by an earlier call: decode nothing
         aborted_at_entry = ld_volatile(reinterpret_cast<const unsigned *>(S.abort_flag)) != 0;
+        // a position past the KV cache / RoPE table, or a token outside the
+        // vocabulary, decodes nothing either: every CTA sees the same values,
+        // so all leave before any load that depends on them, and the word
+        // tells the host why (token and pos are left unchanged).
+        const int p0 = S.pos[0], t0 = S.token[0];
+        if (!aborted_at_entry && (p0 < 0 || p0 >= S.max_ctx || t0 < 0 || t0 >= W.vocab)) {
+            aborted_at_entry = 1;
+            if (blockIdx.x == 0) atomicCAS(S.abort_flag, 0, (p0 < 0 || p0 >= S.max_ctx) ? 2 : 3);
+        }
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(full_bar + 8 * i, 1);
             tc::mbar_init(empty_bar + 8 * i, kPWarps);
@@ -577,7 +586,55 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
             const unsigned hmask = 0xffffu << (threadIdx.x & 16);
             float mx[2] = {-INFINITY, -INFINITY};
-            for (int tb = hw; tb < len; tb += 32 * 4) {
+            if (S.ordered) {
+                // reference order: one thread per (token, query head) runs the
+                // score's whole chain -- 8 fused lanes + add_reduce_mm_256_layer
+                // below 8*(pos/8), 8 unfused lanes added in order in the tail
+                // (layers/src/text_layer.cpp:590-645).  Key rows are staged
+                // through shared memory 64 at a time (rows padded to 272 B).
+                const int tail0 = (pos / 8) * 8;
+                uint4 *kst = reinterpret_cast<uint4 *>(xs + 8 * D);
+                for (int c0 = 0; c0 < len; c0 += 64) {
+                    const int n = min(64, len - c0);
+                    for (int e = threadIdx.x; e < n * 16; e += kPThreads)
+                        kst[(e >> 4) * 17 + (e & 15)] = __ldcg(
+                            reinterpret_cast<const uint4 *>(S.k_pages + kv_off(S, pt_sm, l, t0 + c0 + (e >> 4), kvh)) + (e & 15));
+                    csync();
+                    if (threadIdx.x < 2 * n) {
+                        const int t = c0 + (threadIdx.x >> 1), h = threadIdx.x & 1;
+                        const uint4 *kr = kst + (threadIdx.x >> 1) * 17;
+                        const float *qh = qrot + h * D;
+                        float l8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+                        const bool tail = t0 + t >= tail0;
+#pragma unroll 4
+                        for (int c = 0; c < D / 8; ++c) {
+                            float kf[8];
+                            h8f(kr[c], kf);
+                            if (!tail) {
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) l8[j] = fma_rn(qh[8 * c + j], kf[j], l8[j]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) l8[j] = add_rn(l8[j], mul_rn(qh[8 * c + j], kf[j]));
+                            }
+                        }
+                        float r;
+                        if (!tail) {
+                            r = reduce8_ref(l8);
+                        } else {
+                            r = l8[0];
+#pragma unroll
+                            for (int j = 1; j < 8; ++j) r = add_rn(r, l8[j]);
+                            r = add_rn(0.0f, r);
+                        }
+                        const float sc = mul_rn(r, inv_sqrt_d);
+                        sp[h * kSliceMax + t] = sc;
+                        if (h == 0) mx[0] = fmaxf(mx[0], sc); else mx[1] = fmaxf(mx[1], sc);
+                    }
+                    csync();
+                }
+            }
+            for (int tb = S.ordered ? len : hw; tb < len; tb += 32 * 4) {
                 uint4 kr[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -633,10 +690,12 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 double part = 0.0;
+                float *eh = S.att_e + (size_t)(kvh * 2 + h) * (kSlices * kSliceMax) + t0;
                 for (int t = threadIdx.x; t < len; t += kPThreads) {
                     const float sv = sp[h * kSliceMax + t];
                     const float p = (sv > -INFINITY) ? exp_ref(sv - gm[h]) : 0.0f;
                     sp[h * kSliceMax + t] = p;
+                    if (S.ordered) __stcg(eh + t, p);
                     part += (double)p;
                 }
 #pragma unroll
@@ -649,6 +708,83 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 0; w < kPWarps; ++w) sum += redd[threadIdx.x][w];
                 S.att_lsum[(kvh * 2 + threadIdx.x) * kSlices + sl] = sum;
             }
+            if (S.ordered) {
+                // reference order (layers/src/text_layer.cpp:473-535, 677-689):
+                // once every slice's exponentials are out, each slice CTA takes
+                // 8 output dimensions of both query heads.  The exponentials
+                // are summed into 8 float lanes t-ascending, the lanes then the
+                // tail in double, p = e * (float)(1/sum), and each output
+                // element is one fma chain over t ascending.  E and this CTA's
+                // 16-byte column of V are staged in shared memory (xs) 1024
+                // positions at a time.
+                if (!head_sync(S, kvh)) { drain(); return; }
+                constexpr int kCh = 1024;
+                float *ebuf = xs;                                   // [2][kCh]
+                uint4 *vbuf = reinterpret_cast<uint4 *>(xs + 2 * kCh);   // [kCh] 8 halves each
+                const int d0 = 8 * sl, n8 = (ctx / 8) * 8;
+                const float *e0 = S.att_e + (size_t)(kvh * 2) * (kSlices * kSliceMax);
+                const float *e1 = e0 + kSlices * kSliceMax;
+                auto stage = [&](int c0, int n, bool with_v) {
+                    for (int e = threadIdx.x; e < 2 * n; e += kPThreads)
+                        ebuf[(e >= n) * kCh + (e >= n ? e - n : e)] = __ldcg((e >= n ? e1 + (e - n) : e0 + e) + c0);
+                    if (with_v)
+                        for (int e = threadIdx.x; e < n; e += kPThreads)
+                            vbuf[e] = __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, pt_sm, l, c0 + e, kvh) + d0));
+                    csync();
+                };
+                const bool one = ctx <= kCh;
+                float lane_acc = 0.0f;             // thread h*8+ln: lane ln of head h
+                for (int c0 = 0; c0 < ctx; c0 += kCh) {
+                    const int n = min(kCh, ctx - c0);
+                    stage(c0, n, one);
+                    if (threadIdx.x < 16) {
+                        const float *eb = ebuf + (threadIdx.x >> 3) * kCh;
+                        const int ln = threadIdx.x & 7;
+                        // t = c0 + k with t = ln mod 8 (c0 is a multiple of 8), t < n8
+                        const int kend = min(n, n8 - c0);
+                        for (int k = ln; k < kend; k += 8) lane_acc = add_rn(lane_acc, eb[k]);
+                    }
+                    if (!one) csync();
+                }
+                if (threadIdx.x < 16) scratch[threadIdx.x] = lane_acc;
+                csync();
+                if (threadIdx.x < 2) {
+                    // the tail (at most 7 positions) from global memory
+                    const float *eh = threadIdx.x ? e1 : e0;
+                    double sum = 0.0;
+                    for (int ln = 0; ln < 8; ++ln) sum = __dadd_rn(sum, (double)scratch[threadIdx.x * 8 + ln]);
+                    for (int t = n8; t < ctx; ++t) sum = __dadd_rn(sum, (double)__ldcg(eh + t));
+                    const bool zero = !isfinite(gm[threadIdx.x]) || !(sum > 0.0) || !isfinite(sum);
+                    scratch[32 + threadIdx.x] = zero ? 0.0f : 1.0f;
+                    scratch[34 + threadIdx.x] = __double2float_rn(__ddiv_rn(1.0, sum));
+                }
+                csync();
+                const int h = threadIdx.x >> 3, j = threadIdx.x & 7;
+                const float inv = threadIdx.x < 16 ? scratch[34 + h] : 0.0f;
+                float a = 0.0f;
+                for (int c0 = 0; c0 < ctx; c0 += kCh) {
+                    const int n = min(kCh, ctx - c0);
+                    if (!one) stage(c0, n, true);
+                    if (threadIdx.x < 16) {
+                        const float *eb = ebuf + h * kCh;
+                        const __half *vb = reinterpret_cast<const __half *>(vbuf) + j;
+                        int k = 0;
+                        for (; k + 8 <= n; k += 8) {
+                            float pv[8], vv[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                pv[u] = mul_rn(eb[k + u], inv);
+                                vv[u] = __half2float(vb[(k + u) * 8]);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) a = fma_rn(pv[u], vv[u], a);
+                        }
+                        for (; k < n; ++k) a = fma_rn(mul_rn(eb[k], inv), __half2float(vb[k * 8]), a);
+                    }
+                    if (!one) csync();
+                }
+                if (threadIdx.x < 16) S.att_out[(kvh * 2 + h) * D + d0 + j] = scratch[32 + h] != 0.0f ? a : 0.0f;
+            } else {
             float acc[2][8];
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -728,6 +864,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 }
                 if (threadIdx.x == 0) S.att_cnt[kvh] = 0;     // next used a grid barrier later
             }
+            }   // fast order
         }
         SYNC_OR_EXIT();
 

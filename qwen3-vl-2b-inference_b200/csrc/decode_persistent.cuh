@@ -27,6 +27,8 @@ struct PersistState {
     float *att_lmax;       // [NH][16] slice maxima
     double *att_lsum;      // [NH][16] slice sums
     float *att_pacc;       // [NH][16][D] slice partial outputs
+    float *att_e;          // [NH][16 * 512] exponentials (reference-order mode)
+    int ordered;           // attention in the reference's summation order
     int *att_cnt;          // [NKV] slices finished (zero between layers)
     float *att_out;        // [NH * D] attention output
     float *warp_best_v;    // [grid * 16]

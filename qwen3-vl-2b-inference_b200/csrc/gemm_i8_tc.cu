@@ -34,6 +34,9 @@ constexpr int kThreads = 128;
 constexpr int kUmmaK = 32;        // K per kind::i8 MMA
 }  // namespace
 
+// Set (to 1) when a bounded wait in this kernel gave up; while it is set the
+// kernel computes nothing.  The host reads and clears it through
+// qvl_tc_timeout_word().
 __device__ int g_gemm_tc_timeout = 0;
 
 template <int NT>
@@ -98,7 +101,18 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     const uint32_t d_hi = tmem, d_lo = tmem + NT;
 
     pdl_launch_dependents();
+    // an earlier launch timed out: leave before issuing anything
+    __shared__ int timed_out_at_entry;
+    if (threadIdx.x == 0) timed_out_at_entry = *reinterpret_cast<volatile int *>(&g_gemm_tc_timeout) != 0;
+    __syncthreads();
+    if (timed_out_at_entry) {
+        tc::tc_fence_before();
+        __syncthreads();
+        if (warp == 1) tc::tmem_dealloc(tmem, kCols);
+        return;
+    }
     bool ok = true;
+    int issued = 0;                 // stages the producer issued (producer thread only)
     if (warp == 0 && lane == 0) {
         // ---- TMA producer (weights first: they do not depend on the previous kernel)
         for (int kb = 0; kb < nk && ok; ++kb) {
@@ -111,6 +125,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
             if (kb == 0) pdl_wait();   // activations come from the previous kernel
             tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, (kb0 + kb) * kBK, m0, full0 + 8 * s);
             tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, (kb0 + kb) * kBK, m0, full0 + 8 * s);
+            issued = kb + 1;
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
@@ -201,6 +216,12 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
         }
         cluster.sync();   // partials stay alive until every rank has read them
     }
+    if (warp == 0 && lane == 0 && !ok) {
+        // the producer gave up: wait (bounded) for the copies it already
+        // issued, so none lands in shared memory after the CTA has left
+        for (int kb = issued - 1; kb >= 0 && kb >= issued - kStages; --kb)
+            tc::mbar_wait(full0 + 8 * (kb % kStages), (kb / kStages) & 1, nullptr);
+    }
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 1) tc::tmem_dealloc(tmem, kCols);
@@ -285,6 +306,12 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
 }
 
 }  // namespace
+
+int *gemm_tc_timeout_word() {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemm_tc_timeout) != cudaSuccess) return nullptr;
+    return static_cast<int *>(p);
+}
 
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
     return M >= 16 && g == K && K % kBK == 0 && N >= kBM && (N + kBM - 1) / kBM <= 65535 && get_encode() != nullptr;

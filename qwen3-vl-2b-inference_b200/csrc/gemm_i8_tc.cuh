@@ -7,6 +7,8 @@ namespace qvl {
 // Tensor-core (tcgen05 kind::i8) INT8 GEMM with TILED summation semantics.
 // TILED summation, per-output-row weight scales (g == K), K % 128 == 0, M >= 16.
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g);
+// device address (current device) of the kernel's timeout word, or nullptr
+int *gemm_tc_timeout_word();
 // bytes of the hi/lo activation planes the GEMM needs in the caller's workspace
 size_t gemm_tc_planes_bytes(size_t M, size_t K);
 cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,

@@ -4,10 +4,9 @@
 // (the down linear re-quantises the SwiGLU output,
 // matmul/src/cpu_f32a_i8f32sb_f32c_avx2.cpp:135-177).
 //
-// exp is evaluated in double precision and rounded once to fp32, which gives
-// the correctly rounded expf value (glibc's expf, used by the reference, is
-// correctly rounded for all but a vanishing set of inputs); the add, divide
-// and multiply are IEEE single-precision round-to-nearest like the CPU's.
+// exp is expf_host (common.cuh): the host C library's expf, bit for bit; the
+// add, divide and multiply are IEEE single-precision round-to-nearest like
+// the CPU's.
 #include "common.cuh"
 #include "qact.cuh"
 #include "swiglu.cuh"
@@ -54,6 +53,11 @@ swiglu_quant_kernel(const float *__restrict gate, const float *__restrict up,
     for (int i = threadIdx.x; i < n; i += blockDim.x) q[base + i] = quant_one(hs[i], inv_s[i / g]);
 }
 
+__global__ void expf_host_kernel(const float *__restrict x, float *__restrict y, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        y[i] = expf_host(x[i]);
+}
+
 static void pdl_cfg(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -88,6 +92,12 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int16_t *q, 
     cfg.gridDim = dim3((I / g + gpb - 1) / gpb, M);
     cfg.blockDim = dim3(256);
     return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, q, s, I, g, gpb);
+}
+
+cudaError_t launch_expf_host(const float *x, float *y, long n, cudaStream_t stream) {
+    long blocks = (n + 255) / 256;
+    expf_host_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, stream>>>(x, y, n);
+    return cudaGetLastError();
 }
 
 }  // namespace qvl

@@ -29,6 +29,7 @@ import numpy as np
 import torch
 
 from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Workspace, attention, embedding_lookup_i8,
+               attention_ordered, DECODE_REFERENCE_ORDER,
                attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
                qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct)
 from . import load_library
@@ -107,14 +108,22 @@ class TextDecoder:
     """Batched decode over a paged FP16 KV cache (one sequence per request)."""
 
     def __init__(self, weights: TextWeights, max_batch: int, max_ctx: int, page_size: int = 64,
-                 device="cuda", batch_order: str = "auto", persistent: bool = False):
+                 device="cuda", batch_order: str = "auto", persistent: bool = False,
+                 attn_order: str = "reference"):
         """batch_order: "lane8" computes every request row in the reference's
         M=1 decode order (CUDA-core GEMV, each request bit-matches the
         reference run on it alone); "tiled" runs the batch as one M=B product
         on the tensor cores in the reference's M>1 order (what the reference's
         linear() does for an M>1 call); "auto" = tiled for B >= 16.
         persistent: (max_batch 1 only) run each token as ONE cooperative
-        launch (qvl_text_decode_step) instead of ~6 launches per layer."""
+        launch (qvl_text_decode_step) instead of ~6 launches per layer.
+        attn_order: "fast" splits each context over CTAs (fp32 partial sums
+        grouped differently from the reference); "reference" runs the
+        reference's own summation order, so that with the lane8 order every
+        operation of a token is bit-identical to the reference's."""
+        if attn_order not in ("fast", "reference"):
+            raise ValueError(attn_order)
+        self.attn_order = attn_order
         self.w = weights
         cfg = self.cfg = weights.cfg
         self.B = max_batch
@@ -166,6 +175,8 @@ class TextDecoder:
             self.tc_ws.get(load_library().qvl_linear_q16_i8_batched_workspace_bytes(max_batch, cfg.intermediate))
         self.ws = Workspace(dev)
         self.ws.get(load_library().qvl_attention_workspace_bytes(B, max_ctx, self.kv[0].dims))
+        if attn_order == "reference":
+            self.ws.get(load_library().qvl_attention_ordered_workspace_bytes(B, max_ctx, self.kv[0].dims))
 
     def set_rope_table(self, cos: np.ndarray, sin: np.ndarray):
         self.rope_cos = torch.from_numpy(np.ascontiguousarray(cos)).to(self.device)
@@ -191,7 +202,7 @@ class TextDecoder:
         if self.persistent:
             text_decode_step(self.pw, self.x, self.logits, self.tokens, self.positions, self.k_all, self.v_all,
                              self.kv[0].page_table, self.page_size, self.rope_cos, self.rope_sin, self.max_ctx,
-                             self.pws)
+                             self.pws, flags=DECODE_REFERENCE_ORDER if self.attn_order == "reference" else 0)
             return
         cfg, t = self.cfg, self.w.t
         H, ng, eps = cfg.hidden, cfg.norm_group, cfg.eps
@@ -214,7 +225,10 @@ class TextDecoder:
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
-            if self.fuse_tails:
+            if self.attn_order == "reference":
+                attention_ordered(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+                _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
+            elif self.fuse_tails:
                 attention_q16(self.q[:B], self.kv[l], seq, pos, self.max_ctx, self.att[:B], self.qa[:B],
                               self.qa_s[:B], self.counters[3], workspace=self.ws)
             else:
@@ -267,7 +281,7 @@ class TextDecoder:
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
-            attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+            (attention_ordered if self.attn_order == "reference" else attention)(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
             _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
             linear_batched(self.qa[:B], self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], ws,
                            semantics=SEM_TILED | SEM_ACCUMULATE)

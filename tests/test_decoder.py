@@ -237,3 +237,22 @@ def test_persistent_decode_abort_word(qvl, cuda):
     torch.cuda.synchronize()
     assert not qvl.text_decode_aborted(dec.pws)
     assert int(dec.positions[0].item()) == 4
+
+
+@pytest.mark.parametrize("pos,token,code", [(64, 9, 2), (-1, 9, 2), (3, 1 << 20, 3)])
+def test_persistent_decode_rejects_out_of_range(qvl, cuda, pos, token, code):
+    """A position at or past max_ctx (the KV cache and RoPE table end there),
+    a negative one, or a token outside the vocabulary: the launch decodes
+    nothing, reports the reason in the abort word and leaves token and pos."""
+    import qvl_b200.decoder as D
+    cfg = _small_cfg(D, layers=1)
+    w = D.TextWeights.random(cfg, seed=1, device=cuda)
+    dec = D.TextDecoder(w, max_batch=1, max_ctx=64, device=cuda, persistent=True)
+    dec.tokens[0] = token
+    dec.positions[0] = pos
+    L = qvl.load_library()
+    off = L.qvl_text_decode_abort_flag(dec.pws.data_ptr()) - dec.pws.data_ptr()
+    dec.step()
+    torch.cuda.synchronize()
+    assert int(dec.pws[off:off + 4].view(torch.int32).item()) == code
+    assert int(dec.tokens[0].item()) == token and int(dec.positions[0].item()) == pos

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from test_gpu_parity import NH, NKV, D, _attn_setup, dev, rel_err, REL_TOL_FP32
+from test_gpu_parity import NH, NKV, D, _attn_setup, dev
 
 pytestmark = pytest.mark.gpu
 
@@ -46,13 +46,14 @@ def _run_both(qvl, cuda, ctxs, seed):
 
 
 def test_static_scratch_attention_matches_workspace_path(qvl, cuda):
-    # two calls in a row on different shapes: the second reuses the array the
-    # first one left behind.  Contexts above 8192 tokens with few queries take
-    # the split-K path, the one that uses the scratch.
-    for ctxs, seed in (([9000, 33], 1), ([12000], 2)):
+    # calls in a row on different shapes: each reuses the array the one before
+    # left behind.  Contexts above 8192 tokens with few queries take the
+    # split-K path, the one that uses the scratch; [300, 33] takes the cluster
+    # path.  Both entry points run the same kernels, so the bytes must agree.
+    for ctxs, seed in (([9000, 33], 1), ([12000], 2), ([300, 33], 3), ([9000, 33], 4)):
         got, expect = _run_both(qvl, cuda, ctxs, seed)
-        assert rel_err(got, expect) < REL_TOL_FP32
         assert np.isfinite(got).all()
+        assert np.array_equal(got, expect)
 
 
 def test_static_scratch_rejects_oversized_requests(qvl, cuda):
