@@ -204,6 +204,14 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg,
  * qvl_rope_kv_append: q fp32 [nq, NH, D] rotated in place; k_new, v_new fp32
  * [nq, NKV, D]: k rotated, both rounded to fp16 and written at their position.
  * qvl_attention_decode: out fp32 [nq, NH, D]. */
+/* Host function (no device work): the RoPE table the attention entry points
+ * take, computed as the reference's qwen_rope_precompute computes its text
+ * section (model/src/load_model.cpp:413-490) with the host's single-precision
+ * libm: cos/sin of pos / powf(theta, 2i/head_dim); theta is an integer there
+ * (the header stores rope_theta as int, :71).  cos_out, sin_out: host
+ * float [rows, head_dim/2]. */
+int qvl_rope_table(int theta, int head_dim, int rows, float *cos_out, float *sin_out);
+
 typedef struct {
     int num_heads;          /* NH  (16 for Qwen3-VL-2B)                 */
     int num_kv_heads;       /* NKV (8)                                  */

@@ -20,6 +20,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libqwen_ref.so")
+REF_MODEL_SO = os.path.join(HERE, "_ref", "libqwen_ref_model.so")
+# the same decoder with the product's linear() shim linked in place of the reference's
+REF_B200_SO = os.path.join(HERE, "_ref", "libqwen_ref_b200.so")
 
 
 def _reference_dir():
@@ -107,6 +110,67 @@ def ref_lib():
         L.ref_embedding_i8.argtypes = [_P, _P, _P, _Z, _Z, _Z]
         _ref = L
     return _ref
+
+
+class RefModel:
+    """The reference's own text decoder end to end (oracle/ref_model.cpp):
+    init_model_weights on a .bin model file, qwen_rope_precompute, and
+    forward_text per token; per-row INT8 through the reference's INT8 kernel
+    with group = K, and (fp16_kv) the new KV rows rounded to fp16 values as
+    an FP16 cache holds them.  One model per library at a time.
+
+    dropin=True loads the build whose linear() is the product's host shim
+    (host/linear_shim.cpp): the reference's forward_text with every INT8
+    product on the GPU."""
+
+    _libs: dict = {}
+
+    def __init__(self, path: str, fp16_kv: bool = True, dropin: bool = False):
+        so = REF_B200_SO if dropin else REF_MODEL_SO
+        if so not in RefModel._libs:
+            L = ctypes.CDLL(so)
+            L.refm_load.argtypes = [ctypes.c_char_p, _I]
+            L.refm_load.restype = _I
+            L.refm_config.argtypes = [_P]
+            L.refm_forward.argtypes = [_I, _I]
+            L.refm_forward.restype = ctypes.POINTER(ctypes.c_float)
+            L.refm_rope.argtypes = [_P, _P, _I]
+            L.refm_kv.argtypes = [_I]
+            L.refm_kv.restype = ctypes.POINTER(ctypes.c_float)
+            L.refm_free.argtypes = []
+            RefModel._libs[so] = L
+        L = self._lib = RefModel._libs[so]
+        if L.refm_load(path.encode(), int(fp16_kv)) != 0:
+            raise RuntimeError(f"reference loader failed on {path} (or a model is already loaded)")
+        c = np.zeros(12, np.int32)
+        L.refm_config(c.ctypes.data)
+        self.vocab, self.hidden, self.inter, self.layers, self.heads, self.kv_heads, self.seq_len = map(int, c[:7])
+        self.rope_theta, self.group_size, self.group_quantized = int(c[7]), int(c[9]), int(c[10])
+        self.eps = float(c[11:12].view(np.float32)[0])
+        self.head_dim = self.hidden // self.heads
+        n = self.layers * self.kv_heads * self.seq_len * self.head_dim
+        shape = (self.layers, self.kv_heads, self.seq_len, self.head_dim)
+        self.k_cache = np.ctypeslib.as_array(L.refm_kv(0), shape=(n,)).reshape(shape)
+        self.v_cache = np.ctypeslib.as_array(L.refm_kv(1), shape=(n,)).reshape(shape)
+
+    def rope(self, rows: int):
+        half = self.head_dim // 2
+        c = np.empty((rows, half), np.float32)
+        s = np.empty((rows, half), np.float32)
+        self._lib.refm_rope(c.ctypes.data, s.ctypes.data, rows)
+        return c, s
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        """forward_text: the logits (a copy) for `token` at `pos`."""
+        p = self._lib.refm_forward(int(token), int(pos))
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def close(self):
+        self._lib.refm_free()
+
+
+def ref_model_available() -> bool:
+    return os.path.exists(REF_MODEL_SO)
 
 
 # ---------------------------------------------------------------- restatement

@@ -50,6 +50,7 @@ EXPORTED = (
     "qvl_text_decode_step_ex",
     "qvl_text_decode_abort_flag", "qvl_text_decode_trace", "qvl_tc_timeout_status",
     "qvl_attention_decode_static", "qvl_attention_ordered_workspace_bytes", "qvl_attention_decode_ordered",
+    "qvl_rope_table",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -137,6 +138,7 @@ def load_library(path: str = LIB_PATH):
     L.qvl_text_decode_trace.restype = _P
     L.qvl_text_decode_trace.argtypes = [_P]
     L.qvl_tc_timeout_status.argtypes = [ctypes.POINTER(_I), _I, _P]
+    L.qvl_rope_table.argtypes = [_I, _I, _I, _P, _P]
     L.qvl_internal_set_tc_timeout.argtypes = [_P]
     _lib = L
     return L

@@ -120,6 +120,27 @@ int qvl_last_cuda_error(void) { return g_last_cuda_error; }
 
 const char *qvl_version(void) { return "qvl_b200 0.1"; }
 
+// Host code: the text section of qwen_rope_precompute
+// (model/src/load_model.cpp:413-490) with the host's single-precision libm, as
+// the reference computes it: inv_freq[i] = 1 / powf(theta, 2i / D), then
+// cosf / sinf of pos * inv_freq[i].  For text positions the three M-RoPE
+// sections carry the same position, so the interleave leaves section 0 equal
+// to this table.
+int qvl_rope_table(int theta, int head_dim, int rows, float *cos_out, float *sin_out) {
+    if (!cos_out || !sin_out || head_dim <= 0 || head_dim % 2 || rows < 0) return QVL_ERR_INVALID;
+    const int half = head_dim / 2;
+    for (int i = 0; i < half; ++i) {
+        const volatile float e = (2.0f * (float)i) / (float)head_dim;
+        const float inv_freq = 1.0f / powf((float)theta, e);
+        for (int p = 0; p < rows; ++p) {
+            const volatile float f = (float)p * inv_freq;
+            cos_out[(size_t)p * half + i] = cosf(f);
+            sin_out[(size_t)p * half + i] = sinf(f);
+        }
+    }
+    return QVL_OK;
+}
+
 int qvl_tc_timeout_status(int *timed_out, int clear, void *stream) {
     if (!timed_out) return QVL_ERR_INVALID;
     int *word = qvl::gemm_tc_timeout_word();

@@ -50,14 +50,18 @@ class TextConfig:
 
 
 def rope_table(max_pos: int, head_dim: int = 128, theta: float = 5e6):
-    """Text section of qwen_rope_precompute (model/src/load_model.cpp:428-472):
-    cos/sin of pos * 1/theta^(2i/D), computed on the host in float32."""
-    i = np.arange(head_dim // 2, dtype=np.float32)
-    inv_freq = (np.float32(1.0) / np.power(np.float32(theta), (np.float32(2.0) * i) / np.float32(head_dim),
-                                           dtype=np.float32)).astype(np.float32)
-    pos = np.arange(max_pos, dtype=np.float32)[:, None]
-    f = (pos * inv_freq[None, :]).astype(np.float32)
-    return np.cos(f).astype(np.float32), np.sin(f).astype(np.float32)
+    """Text section of qwen_rope_precompute (model/src/load_model.cpp:413-490),
+    computed on the host by qvl_rope_table with the host's single-precision
+    libm exactly as the reference computes it (theta is an integer there)."""
+    import ctypes
+    c = np.empty((max_pos, head_dim // 2), np.float32)
+    s = np.empty((max_pos, head_dim // 2), np.float32)
+    L = load_library()
+    rc = L.qvl_rope_table(int(theta), head_dim, max_pos, c.ctypes.data_as(ctypes.c_void_p),
+                          s.ctypes.data_as(ctypes.c_void_p))
+    if rc:
+        raise ValueError(f"qvl_rope_table: status {rc}")
+    return c, s
 
 
 _MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")

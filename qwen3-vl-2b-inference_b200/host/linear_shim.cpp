@@ -11,7 +11,14 @@
 // every call.  The workspace is allocated once and grown when needed, at the
 // first call of a size, never on a repeated shape.
 //
-// Build (the reference links it in place of its own INT8 branch):
+// The definition is the reference's own symbol: global `linear` with the
+// reference's `struct DType { enum Type ... }` (utils/include/tensor.hpp:25-27)
+// mangles to the same name, so an object linked in place of the reference's
+// (or ahead of a weakened copy of it) serves every call site unchanged --
+// forward_text (model/src/forward.cpp:506-654) and classifier_gemm
+// (layers/src/text_layer.cpp:309-313) included.
+//
+// Build:
 //   g++ -std=c++17 -O2 -fPIC -I include -c linear_shim.cpp
 //   ... -L qwen3-vl-2b-inference_b200/lib -lqvl_b200 -lcudart
 #include <cstdio>
@@ -22,11 +29,12 @@
 #include <cuda_runtime.h>
 #include "qvl_b200.h"
 
-namespace qvl_shim {
-
-// The reference's DType enum (utils/include/tensor.hpp:25-27), same values.
+// The reference's DType (utils/include/tensor.hpp:25-27): same name, same
+// enumerators and values, so `linear` below has the reference's mangled name.
 struct DType { enum Type { FP32 = QVL_DTYPE_FP32, INT32 = QVL_DTYPE_INT32, FP16 = QVL_DTYPE_FP16,
                            INT8 = QVL_DTYPE_INT8, INT4 = QVL_DTYPE_INT4 }; };
+
+namespace qvl_shim {
 
 std::mutex g_mu;
 struct Mirror {
@@ -72,10 +80,13 @@ void grow(void **p, size_t *have, size_t need) {
 }
 }  // namespace
 
+}  // namespace qvl_shim
+
 void linear(const void *mat_A, const void *mat_B_in, const void *mat_B_scale, const void *mat_bias_in,
             const void *mat_bias_scale, void *mat_C, size_t M, size_t N, size_t K, bool mat_B_transpose,
             DType::Type type_a, DType::Type type_b, DType::Type type_b_scale, DType::Type type_c,
             bool group_quantized, size_t group_size) {
+    using namespace qvl_shim;
     (void)mat_bias_scale;
     if (!(type_a == DType::FP32 && type_c == DType::FP32 && type_b == DType::INT8 &&
           type_b_scale == DType::FP32 && mat_bias_in == nullptr && mat_B_transpose)) {
@@ -102,8 +113,6 @@ void linear(const void *mat_A, const void *mat_B_in, const void *mat_B_scale, co
     check(cudaMemcpy(mat_C, g_c, M * N * sizeof(float), cudaMemcpyDeviceToHost), "result");
 }
 
-}  // namespace qvl_shim
-
 // Frees every device weight copy (call when the host weights are unmapped).
 extern "C" void qvl_shim_release_weights(void) {
     std::lock_guard<std::mutex> lock(qvl_shim::g_mu);
@@ -114,7 +123,6 @@ extern "C" void qvl_shim_release_weights(void) {
 // C entry used by the tests (ctypes) to drive the C++ shim.
 extern "C" void qvl_shim_linear_i8(const float *A, const int8_t *B, const float *Bs, float *C, size_t M,
                                    size_t N, size_t K, int group_quantized, size_t group_size) {
-    qvl_shim::linear(A, B, Bs, nullptr, nullptr, C, M, N, K, true, qvl_shim::DType::FP32,
-                     qvl_shim::DType::INT8, qvl_shim::DType::FP32, qvl_shim::DType::FP32,
-                     group_quantized != 0, group_size);
+    linear(A, B, Bs, nullptr, nullptr, C, M, N, K, true, DType::FP32, DType::INT8, DType::FP32, DType::FP32,
+           group_quantized != 0, group_size);
 }

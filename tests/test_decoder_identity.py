@@ -105,3 +105,48 @@ def test_full_depth_greedy_identity(qvl, cuda, seed):
         tok = int(ref_tok)
         ids.append(tok)
     assert len(set(ids)) > 1
+
+
+def test_model_file_end_to_end_vs_reference_forward_text(qvl, cuda, tmp_path):
+    """A full-size model file in the exporter's layout (synthetic int8
+    weights, per-row scales) read to the GPU by qvl_b200.modelfile and, on
+    the host, by the reference's own init_model_weights; then the reference's
+    own forward_text (FP16-valued KV rows) against both GPU engines over 32
+    greedy tokens after a 452-position prompt state: logits bit-identical."""
+    import qvl_b200.decoder as D
+    import qvl_b200.modelfile as MF
+    if not oracle.ref_model_available():
+        pytest.skip("reference model library (oracle/_ref) not built")
+    hdr = MF.qwen3vl_2b_header(vision_hidden_size=32, vision_intermediate_size=64, vision_num_heads=2)
+    path = str(tmp_path / "qwen3vl2b_text_rowwise.bin")
+    MF.write_model_bin(path, hdr, MF.synthetic_text(hdr, seed=5))
+    cfg, w = MF.load_text_weights(path, device=cuda)
+    assert (cfg.layers, cfg.vocab, cfg.hidden, cfg.norm_group) == (28, 151936, 2048, 128)
+    rm = oracle.RefModel(path, fp16_kv=True)
+    try:
+        max_ctx, ctx0, steps = 1024, 452, 32
+        chain, pers = _engines(D, w, max_ctx, ctx0, 11, cuda, [(False, "reference"), (True, "reference")])
+        rc, rs = rm.rope(max_ctx)
+        assert np.array_equal(chain.rope_cos.cpu().numpy(), rc) and np.array_equal(chain.rope_sin.cpu().numpy(), rs)
+        pt = chain.kv[0].page_table[0].long()
+        for l in range(cfg.layers):
+            kk = chain.kv[l].k[pt].float().cpu().numpy().transpose(1, 0, 2, 3).reshape(cfg.kv_heads, -1, cfg.head_dim)
+            vv = chain.kv[l].v[pt].float().cpu().numpy().transpose(1, 0, 2, 3).reshape(cfg.kv_heads, -1, cfg.head_dim)
+            rm.k_cache[l, :, :ctx0] = kk[:, :ctx0]
+            rm.v_cache[l, :, :ctx0] = vv[:, :ctx0]
+        tok = 2024
+        for d in (chain, pers):
+            d.tokens[0] = tok
+        for s in range(steps):
+            for d in (chain, pers):
+                d.step()
+            torch.cuda.synchronize()
+            ref_logits = rm.forward(tok, ctx0 + s)
+            ref_tok = oracle.argmax(ref_logits)
+            for name, d in (("chain", chain), ("persistent", pers)):
+                got = d.logits[0].cpu().numpy()
+                assert np.array_equal(got, ref_logits), (s, name, float(np.abs(got - ref_logits).max()))
+                assert int(d.tokens[0].item()) == ref_tok, (s, name)
+            tok = ref_tok
+    finally:
+        rm.close()

@@ -24,7 +24,9 @@ def _shim():
 def test_shim_library_exports_linear():
     L = _shim()
     assert hasattr(L, "qvl_shim_linear_i8")
-    assert hasattr(L, "_ZN8qvl_shim6linearEPKvS1_S1_S1_S1_PvmmmbNS_5DType4TypeES4_S4_S4_bm")
+    # the reference's own mangled name of linear() (its global `linear` with
+    # `struct DType`), so reference objects bind to it at link time
+    assert hasattr(L, "_Z6linearPKvS0_S0_S0_S0_PvmmmbN5DType4TypeES3_S3_S3_bm")
 
 
 @pytest.mark.gpu
@@ -45,3 +47,46 @@ def test_shim_matches_reference_linear(cuda, M, N, K, gq, g):
         np.testing.assert_array_equal(y, ref)
     # the host weights go away with this test: drop their device copies
     L.qvl_shim_release_weights()
+
+
+def _ref_object_symbol(name):
+    """Mangled names the reference's compiled forward_text object references."""
+    import subprocess
+    obj = os.path.join(os.path.dirname(oracle.REF_SO), "obj", "model", "src", "forward.o")
+    if not os.path.exists(obj):
+        pytest.skip("reference objects not built")
+    out = subprocess.run(["nm", "-u", obj], capture_output=True, text=True, check=True).stdout
+    return name in out
+
+
+def test_reference_call_sites_bind_to_the_shim_symbol():
+    """The reference's forward_text object calls exactly the symbol the shim
+    defines."""
+    assert _ref_object_symbol("_Z6linearPKvS0_S0_S0_S0_PvmmmbN5DType4TypeES3_S3_S3_bm")
+
+
+@pytest.mark.gpu
+def test_reference_forward_text_on_the_shim(qvl, cuda, tmp_path):
+    """The reference's own decoder (loader, forward_text, classifier_gemm)
+    linked with the shim in place of its linear(): every INT8 product runs on
+    the B200 kernels and the logits equal the reference's CPU build (per-row
+    products through its own kernel with group K) bit for bit."""
+    import qvl_b200.modelfile as MF
+    if not (os.path.exists(oracle.REF_B200_SO) and oracle.ref_model_available()):
+        pytest.skip("reference model libraries not built")
+    hdr = MF.qwen3vl_2b_header(num_hidden_layers=2, vision_hidden_size=32, vision_intermediate_size=64,
+                               vision_num_heads=2)
+    p = str(tmp_path / "m.bin")
+    MF.write_model_bin(p, hdr, MF.synthetic_text(hdr, seed=9))
+    gpu = oracle.RefModel(p, fp16_kv=False, dropin=True)
+    cpu = oracle.RefModel(p, fp16_kv=False)
+    try:
+        tok = 99
+        for pos in range(6):
+            a = gpu.forward(tok, pos)
+            b = cpu.forward(tok, pos)
+            np.testing.assert_array_equal(a, b, err_msg=f"pos {pos}")
+            tok = oracle.argmax(b)
+    finally:
+        gpu.close()
+        cpu.close()
