@@ -603,17 +603,29 @@ def run_prefill(args):
         dist.init_process_group("nccl", device_id=dev)
     cfg = D.TextConfig()
     T = PROMPT_CTX
-    w = D.TextWeights.random(cfg, seed=rank, device=dev)
-    dec = D.TextDecoder(w, max_batch=1, max_ctx=T + 8, device=dev)
+    tp = args.tp and ws > 1
+    # tensor split: every rank holds the same weights and prompt and computes
+    # its output columns of every product; replicas: one prompt per rank
+    seed = 0 if tp else rank
+    w = D.TextWeights.random(cfg, seed=seed, device=dev)
+    dec = D.TextDecoder(w, max_batch=1, max_ctx=T + 8, device=dev, tp_group=dist.group.WORLD if tp else None)
     prompt = torch.randint(0, 151643, (T,), dtype=torch.int32, device=dev,
-                           generator=torch.Generator(device=dev).manual_seed(rank))
+                           generator=torch.Generator(device=dev).manual_seed(seed))
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         dec.prefill(prompt)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            dec.prefill(prompt)
+        if tp:
+            # the tensor-split pass runs eagerly (NCCL collectives are not
+            # captured); one pass is ~600 launches, far below its 10+ ms
+            class _Eager:
+                def replay(self):
+                    dec.prefill(prompt)
+            g = _Eager()
+        else:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                dec.prefill(prompt)
         for _ in range(args.warmup):
             g.replay()
         torch.cuda.synchronize()
@@ -640,12 +652,16 @@ def run_prefill(args):
             tps, n, dt = cpu_decode_rate(args, seconds=args.cpu_seconds)
             cpu = {"value": round(tps, 3), "unit": "prompt tokens/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"{n} prompt tokens fed one at a time as the reference does ({dt * 1e3:.1f} ms each)"}
+        prompts = 1 if tp else ws
         print(json.dumps({
-            "metric": "prefill_tokens_per_s", "value": round(T * ws * args.steps / (ms / 1e3), 1),
+            "metric": "prefill_tokens_per_s", "value": round(T * prompts * args.steps / (ms / 1e3), 1),
             "unit": "prompt tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ttft_ms, "ttft_ms": ttft_ms, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ttft_ms, "ttft_ms": ttft_ms, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic (random ids, random-init weights)",
-            "config": {"workload": f"qwen3vl2b_text_prefill_T{T}", "order": "M=T tensor-core products (reference M>1 order)"},
+            "config": {"workload": f"qwen3vl2b_text_prefill_T{T}", "order": "M=T tensor-core products (reference M>1 order)",
+                       "parallelism": (f"tp{ws}: every product split by output column, NCCL all-gather"
+                                       if tp else f"dp{ws} (one prompt per rank)")},
             "clocks": clk.summary(), "cpu_baseline": cpu,
         }))
     if ws > 1:
@@ -736,14 +752,17 @@ def run_ours(args):
             e1.record(stream)
             torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
+        per_rank = [ms]
         if ws > 1:
             t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+            parts = [torch.empty_like(t) for _ in range(ws)]
+            dist.all_gather(parts, t)
+            per_rank = [float(p.item()) for p in parts]
+            ms = max(per_rank)
+        return ms, per_rank
 
     with ClockSampler(local) as clk:
-        ms = timed()
+        ms, per_rank_ms = timed()
     ms_step = ms / args.steps
     value = B * ws * args.steps / (ms / 1e3)
     # weights streamed per step + KV read per step (fp16, mean context)
@@ -852,6 +871,7 @@ def run_ours(args):
                            else "lane8 (each request in the reference M=1 order)"),
             "roofline": roofline,
             "step_hbm_gbs": round(step_gbs, 1),
+            "per_rank_tokens_per_s": [round(B * args.steps / (m / 1e3), 1) for m in per_rank_ms],
             "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B},
             "gpu_launches": launches,
@@ -876,6 +896,8 @@ def main():
                     choices=["decode", "prefill", "prefill_gemm", "gemv", "attention", "swiglu"])
     ap.add_argument("--attn-order", default="reference", choices=["reference", "fast"],
                     help="decode attention: the reference's summation order (bit-identical logits) or split context")
+    ap.add_argument("--tp", action="store_true",
+                    help="prefill: split every product of one prompt by output column over the ranks")
     ap.add_argument("--batch32-steps", type=int, default=32, help="steps of the batch-32 figure (0: skip)")
     ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
                     help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")

@@ -113,7 +113,7 @@ class TextDecoder:
 
     def __init__(self, weights: TextWeights, max_batch: int, max_ctx: int, page_size: int = 64,
                  device="cuda", batch_order: str = "auto", persistent: bool = False,
-                 attn_order: str = "reference"):
+                 attn_order: str = "reference", tp_group=None):
         """batch_order: "lane8" computes every request row in the reference's
         M=1 decode order (CUDA-core GEMV, each request bit-matches the
         reference run on it alone); "tiled" runs the batch as one M=B product
@@ -124,7 +124,13 @@ class TextDecoder:
         attn_order: "fast" splits each context over CTAs (fp32 partial sums
         grouped differently from the reference); "reference" runs the
         reference's own summation order, so that with the lane8 order every
-        operation of a token is bit-identical to the reference's."""
+        operation of a token is bit-identical to the reference's.
+        tp_group: a torch.distributed group (NCCL) whose ranks run prefill()
+        together: every product of the prompt pass is split by output column
+        over the group and all-gathered (qvl_b200.parallel), so each column
+        is computed once, by its owner, with unchanged arithmetic -- results
+        are bit-identical to one GPU.  Decode steps stay per-rank."""
+        self.tp = tp_group
         if attn_order not in ("fast", "reference"):
             raise ValueError(attn_order)
         self.attn_order = attn_order
@@ -334,28 +340,103 @@ class TextDecoder:
         sq, ps = pf["seq"][:T], pf["pos"][:T]
         ws = pf["ws"]
         embedding_lookup_i8(t["embed"], t["embed_s"], tokens.to(torch.int32), x)
+        prod = self._prefill_product
         for l in range(cfg.layers):
             rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
-            linear_batched(qh, qs, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
-                           [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
+            prod(qh, qs, ("wq", "wk", "wv"), l, [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
             qknorm_rope_kv_append(pf["q"][:T], pf["k"][:T], pf["v"][:T], self.kv[l], sq, ps, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
             attention(pf["q"][:T], self.kv[l], sq, ps, self.max_ctx, out=pf["att"][:T], workspace=ws)
             _quantize_into(pf["att"][:T], qh, qs)
-            linear_batched(qh, qs, [(t["wo"][l], t["wo_s"][l])], [x], ws, semantics=SEM_TILED | SEM_ACCUMULATE)
+            prod(qh, qs, ("wo",), l, [x], ws, acc=True)
             rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
-            linear_batched(qh, qs, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
-                           [pf["gate"][:T], pf["up"][:T]], ws, swiglu_pair=True, up_scratch=pf["up"][:T])
+            prod(qh, qs, ("wg", "wu"), l, [pf["gate"][:T], pf["up"][:T]], ws, swiglu=True, up_scratch=pf["up"][:T])
             _quantize_into(pf["gate"][:T], q16, qs)
-            linear_batched(q16, qs, [(t["wd"][l], t["wd_s"][l])], [x], ws, semantics=SEM_TILED | SEM_ACCUMULATE)
+            prod(q16, qs, ("wd",), l, [x], ws, acc=True)
         last = x[T - 1:T]
         rms_norm_i8(last, t["final_norm"], t["final_norm_s"], ng, eps, out=last, q=qh[:1], q_scales=qs[:1],
                     quant_group=H, inplace_form=True)
-        linear_q16(qh[:1], qs[:1], t["embed"], t["embed_s"], H, C=pf["logits"], semantics=SEM_LANE8)
+        if self.tp is None:
+            linear_q16(qh[:1], qs[:1], t["embed"], t["embed_s"], H, C=pf["logits"], semantics=SEM_LANE8)
+            greedy_decode(pf["logits"], out=self.tokens[seq:seq + 1])
+        else:
+            # LM head split by vocabulary rows; the greedy token from an
+            # 8-byte (value, index) exchange per rank, the logits gathered
+            from . import parallel as par
+            a, b = par.shard_rows(cfg.vocab, self._tp_world, self._tp_rank)
+            loc = self._tp_buf(("lm", b - a), (1, b - a))
+            linear_q16(qh[:1], qs[:1], t["embed"][a:b], t["embed_s"][a:b], H, C=loc, semantics=SEM_LANE8)
+            self.tokens[seq:seq + 1].copy_(par.split_greedy(loc, a, self.tp).to(torch.int32))
+            pf["logits"].copy_(par.gather_columns(loc, cfg.vocab, self.tp))
         self.logits[seq].copy_(pf["logits"][0])
-        greedy_decode(pf["logits"], out=self.tokens[seq:seq + 1])
         self.positions[seq:seq + 1].fill_(start + T)
+
+    @property
+    def _tp_world(self):
+        import torch.distributed as dist
+        return dist.get_world_size(self.tp)
+
+    @property
+    def _tp_rank(self):
+        import torch.distributed as dist
+        return dist.get_rank(self.tp)
+
+    def _tp_buf(self, key, shape, dtype=torch.float32):
+        bufs = self.__dict__.setdefault("_tp_bufs", {})
+        b = bufs.get(key)
+        if b is None or b.numel() < int(np.prod(shape)):
+            b = bufs[key] = torch.empty(int(np.prod(shape)), dtype=dtype, device=self.device)
+        return b[:int(np.prod(shape))].view(shape)
+
+    def _prefill_product(self, q, qs, names, l, outs, ws, acc=False, swiglu=False, up_scratch=None):
+        """outs[i] (+)= q . dequant(W_names[i])^T for the prompt rows, one
+        tensor-core product per matrix in the reference's M>1 order; with a
+        tp group, split by output column and all-gathered (bit-identical)."""
+        t = self.w.t
+        mats = [(t[n][l], t[n + "_s"][l]) for n in names]
+        if self.tp is None:
+            linear_batched(q, qs, mats, outs, ws, semantics=SEM_TILED | (SEM_ACCUMULATE if acc else 0),
+                           swiglu_pair=swiglu, up_scratch=up_scratch)
+            return
+        import torch.distributed as dist
+        from . import parallel as par
+        G, r = self._tp_world, self._tp_rank
+        M = q.shape[0]
+        local, spans = [], []
+        for i, (W, S) in enumerate(mats):
+            a, b = par.shard_rows(W.shape[0], G, r)
+            spans.append((a, b))
+            local.append(self._tp_buf(("out", i), (M, b - a)))
+        up_loc = local[1] if swiglu else None
+        linear_batched(q, qs, [(W[a:b], S[a:b]) for (W, S), (a, b) in zip(mats, spans)], local, ws,
+                       semantics=SEM_TILED, swiglu_pair=swiglu, up_scratch=up_loc)
+        outs = outs[:1] if swiglu else outs        # SwiGLU: only h (in gate's slot) is needed
+        local = local[:len(outs)]
+        if all(o.shape[1] % G == 0 for o in outs):
+            # one all-gather for all the products of this input: rank slices
+            # packed side by side, [G, M, sum of slice widths]
+            widths = [l_.shape[1] for l_ in local]
+            wsum = sum(widths)
+            pack = self._tp_buf(("pack",), (M, wsum))
+            c0 = 0
+            for l_ in local:
+                pack[:, c0:c0 + l_.shape[1]].copy_(l_)
+                c0 += l_.shape[1]
+            buf = self._tp_buf(("gather",), (G, M, wsum))
+            dist.all_gather_into_tensor(buf, pack, group=self.tp)
+            c0 = 0
+            fulls = []
+            for out, w in zip(outs, widths):
+                fulls.append(buf[:, :, c0:c0 + w].permute(1, 0, 2).reshape(M, out.shape[1]))
+                c0 += w
+        else:
+            fulls = [par.gather_columns(l_, o.shape[1], self.tp) for l_, o in zip(local, outs)]
+        for out, full in zip(outs, fulls):
+            if acc:
+                out.add_(full)          # the reference's add_vector after the product
+            else:
+                out.copy_(full)
 
     # launches of our kernels per step (attention = 3 kernels)
     def kernels_per_step(self):
