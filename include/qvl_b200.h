@@ -389,6 +389,53 @@ int *qvl_text_decode_abort_flag(void *workspace);
  * opening of grid barrier i (5 per layer + 1 barriers per token). */
 const uint64_t *qvl_text_decode_trace(const void *workspace);
 
+/* ---- vision tower (FP16 weights; forward_img, model/src/forward.cpp:3-456)
+ * fp16 tensors are passed as uint16_t.  Token-major layouts throughout:
+ * activations [T, features], attention q/k/v/out [T, heads, head_dim] (the
+ * reference's transposes to head-major, tensor_transpose, are folded into the
+ * attention's indexing).  Parity with the reference is by tolerance. */
+
+/* Host functions (no device work).  qvl_vision_rot_table: the per-patch 2-D
+ * rotary tables of qwen_vision_rope_precompute + vision_rot_pos_emb
+ * (model/src/load_model.cpp:492-540, layers/src/vision_layer.cpp:506-623)
+ * with the host libm, fp16, in merge order: cos/sin [grid_h*grid_w,
+ * head_dim].  qvl_vision_pos_interp: the 4 taps (indices into the
+ * num_grid_per_side^2 learned table) and bilinear weights of each patch in
+ * merge order, as vision_pos_embed computes them (vision_layer.cpp:219-504):
+ * idx int32 [T, 4], w float [T, 4]. */
+int qvl_vision_rot_table(float theta, int head_dim, int grid_h, int grid_w, int merge, uint16_t *cos_out,
+                         uint16_t *sin_out);
+int qvl_vision_pos_interp(int grid_h, int grid_w, int num_grid_per_side, int merge, int32_t *idx_out,
+                          float *w_out);
+
+/* conv_3d (vision_layer.cpp:3-217) as a product: x fp32 [T, VH] =
+ * patches fp32 [T, Kp] . w fp16 [VH, Kp]^T + b fp16 [VH]. */
+int qvl_vision_patch_embed(const float *patches, const uint16_t *w, const uint16_t *b, float *x, int T, int VH,
+                           int Kp, void *stream);
+/* vision_pos_embed + add_vector: x[t] += fp16(sum_k pos_w[idx[t][k]] * w[t][k]). */
+int qvl_vision_pos_add(float *x, const uint16_t *pos_w, const int32_t *idx, const float *wts, int T, int VH,
+                       void *stream);
+/* layer_norm (vision_layer.cpp:625-724): rows of H values, fp32 or fp16 in
+ * and out (x_f16, out_f16), fp16 gamma / beta. */
+int qvl_layer_norm(const void *x, int x_f16, const uint16_t *gamma, const uint16_t *beta, void *out, int out_f16,
+                   int rows, int H, float eps, void *stream);
+/* FP16 tensor-core product with bias, replacing linear() with FP16 weights
+ * (matmul/src/cpu_fp16_full_avx2.cpp, cpu_wrapper.cpp:359-390):
+ * C[M, N] = A[M, K] . W[N, K]^T + bias, fp32 accumulation; mode 0: C fp16,
+ * 1: C fp16 after gelu_tanh of the fp16 value (the in-place gelu_tanh that
+ * follows the vision MLP's first linear), 2: C fp32, 3: C fp32 += the fp16
+ * value (linear then add_vector into the residual stream).  N >= 128,
+ * K % 64 == 0, 16-byte aligned rows. */
+int qvl_gemm_f16(const uint16_t *A, const uint16_t *W, const uint16_t *bias, void *C, size_t M, size_t N, size_t K,
+                 int mode, void *stream);
+/* vision_apply_rotary_inplace (vision_layer.cpp:726-776) on x [T, NH, HD]. */
+int qvl_vision_rotary(uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t, int T, int NH, int HD,
+                      void *stream);
+/* vision_att (vision_layer.cpp:821-867): full attention per head, fp32
+ * scores times `scale`, exp256_ps softmax, fp16 out; HD = 64, T <= 2048. */
+int qvl_vision_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out, int T, int NH,
+                         int HD, float scale, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -138,6 +138,8 @@ class RefModel:
             L.refm_kv.argtypes = [_I]
             L.refm_kv.restype = ctypes.POINTER(ctypes.c_float)
             L.refm_free.argtypes = []
+            L.refm_forward_img.argtypes = [_P, _I, _I, _I, _P, _P]
+            L.refm_forward_img.restype = _I
             RefModel._libs[so] = L
         L = self._lib = RefModel._libs[so]
         if L.refm_load(path.encode(), int(fp16_kv)) != 0:
@@ -164,6 +166,19 @@ class RefModel:
         """forward_text: the logits (a copy) for `token` at `pos`."""
         p = self._lib.refm_forward(int(token), int(pos))
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def forward_img(self, patches: np.ndarray, grid_h: int, grid_w: int, out_hidden: int = 2048):
+        """forward_img on preprocessed patches [T, C*2*P*P]: (image embeddings
+        [T/4, out_hidden] fp32, deep-stack rows [3, T/4, hidden] as float)."""
+        patches = np.ascontiguousarray(patches, dtype=np.float32)
+        T = patches.shape[0]
+        d = T // 4
+        x = np.zeros((d, out_hidden), np.float32)
+        deep = np.zeros((3, d, self.hidden), np.float32)
+        r = self._lib.refm_forward_img(patches.ctypes.data, T, grid_h, grid_w, x.ctypes.data, deep.ctypes.data)
+        if r != d:
+            raise RuntimeError("forward_img failed")
+        return x, deep
 
     def close(self):
         self._lib.refm_free()

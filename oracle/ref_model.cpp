@@ -149,6 +149,35 @@ void refm_rope(float *cos_out, float *sin_out, int rows) {
     memcpy(sin_out, g_st.sin_tensor->ptr(), (size_t)rows * half * sizeof(float));
 }
 
+// forward_img (model/src/forward.cpp:3-456) on preprocessed patches
+// [n_patches, C*T*P*P] (copied: forward_img frees its input); then the merged
+// image embeddings [d_tokens, out_hidden] (vision_x, fp32) into out_x and the
+// three deep-stack rows [3][d_tokens][hidden] (fp16 in the reference) as
+// float into out_deep.  Returns d_tokens, or -1.
+int refm_forward_img(const float *patches, int n_patches, int grid_h, int grid_w, float *out_x, float *out_deep) {
+    if (!g_loaded) return -1;
+    const size_t kp = (size_t)g_cfg.vision_num_channels * g_cfg.vision_temporal_patch_size *
+                      g_cfg.vision_patch_size * g_cfg.vision_patch_size;
+    float *img = (float *)malloc((size_t)n_patches * kp * sizeof(float));
+    if (!img) return -1;
+    memcpy(img, patches, (size_t)n_patches * kp * sizeof(float));
+    {
+        QuietStdout quiet;
+        forward_img(&g_cfg, &g_st, &g_w, img, n_patches, (int)kp, grid_h, grid_w);
+    }
+    const int m = g_cfg.vision_spatial_merge_size;
+    const int d_tokens = n_patches / (m * m);
+    const size_t oh = (size_t)g_cfg.out_hidden_size, H = (size_t)g_cfg.hidden_size;
+    memcpy(out_x, g_st.vision_x->ptr(), (size_t)d_tokens * oh * sizeof(float));
+    const size_t vnp_max = g_st.vision_deep_stack->shape[1];
+    const half_float::half *ds = (const half_float::half *)g_st.vision_deep_stack->ptr();
+    for (int d = 0; d < g_cfg.vision_deep_stack_depth; ++d)
+        for (int i = 0; i < d_tokens; ++i)
+            for (size_t j = 0; j < H; ++j)
+                out_deep[((size_t)d * d_tokens + i) * H + j] = (float)ds[((size_t)d * vnp_max + i) * H + j];
+    return d_tokens;
+}
+
 // Releases the model so that another file can be loaded (the mapped weight
 // files stay mapped: the reference's destructor unmaps an unaligned address).
 void refm_free(void) {

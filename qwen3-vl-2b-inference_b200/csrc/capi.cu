@@ -11,6 +11,7 @@
 #include "gemv_ring.cuh"
 #include "swiglu.cuh"
 #include "attention_ordered.cuh"
+#include "gemm_f16_tc.cuh"
 #include "attention.cuh"
 #include "argmax.cuh"
 #include "norm.cuh"
@@ -143,15 +144,15 @@ int qvl_rope_table(int theta, int head_dim, int rows, float *cos_out, float *sin
 
 int qvl_tc_timeout_status(int *timed_out, int clear, void *stream) {
     if (!timed_out) return QVL_ERR_INVALID;
-    int *word = qvl::gemm_tc_timeout_word();
-    if (!word) return QVL_ERR_CUDA;
+    int *words[2] = {qvl::gemm_tc_timeout_word(), qvl::gemm_f16_timeout_word()};
+    if (!words[0] || !words[1]) return QVL_ERR_CUDA;
     cudaStream_t st = (cudaStream_t)stream;
-    int v = 0;
-    QVL_CUDA_TRY(cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, st));
+    int v[2] = {0, 0};
+    for (int i = 0; i < 2; ++i) QVL_CUDA_TRY(cudaMemcpyAsync(&v[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, st));
     QVL_CUDA_TRY(cudaStreamSynchronize(st));
-    *timed_out = v != 0;
-    if (clear && v) {
-        QVL_CUDA_TRY(cudaMemsetAsync(word, 0, sizeof(int), st));
+    *timed_out = (v[0] | v[1]) != 0;
+    if (clear && *timed_out) {
+        for (int i = 0; i < 2; ++i) QVL_CUDA_TRY(cudaMemsetAsync(words[i], 0, sizeof(int), st));
         QVL_CUDA_TRY(cudaStreamSynchronize(st));
     }
     return QVL_OK;

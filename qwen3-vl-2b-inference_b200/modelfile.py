@@ -177,14 +177,40 @@ def write_model_bin(path: str, header: dict, text: dict, vision_bits: int = 16, 
             f.write(scales.tobytes())
             f.write(data.tobytes())
         fdt = np.float16 if vision_bits == 16 else np.float32
-        for shape in vision_shapes(hdr):
-            f.write((rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * 0.02).astype(fdt).tobytes())
+        for name, shape in vision_tensors(hdr):
+            f.write(_vision_init(name, shape, rng).astype(fdt).tobytes())
+
+
+_VISION_ORDER = ("patch_b", "patch_w", "pos_w", "proj_b", "proj_w", "qkv_b", "qkv_w", "mlp1_b", "mlp1_w",
+                 "mlp2_b", "mlp2_w", "norm1_b", "norm1_w", "norm2_b", "norm2_w", "d_mlp1_b", "d_mlp1_w",
+                 "d_mlp2_b", "d_mlp2_w", "d_norm_b", "d_norm_w", "merge_mlp1_b", "merge_mlp1_w",
+                 "merge_mlp2_b", "merge_mlp2_w", "merge_norm_b", "merge_norm_w")
+
+
+def vision_tensors(h: dict):
+    """(name, shape) of the vision-tower tensors in file order
+    (load_model.cpp:199-246; 2304 position embeddings, 3 channels and 3
+    deep-stack mergers are fixed there).  Matrices keep the exporter's
+    [out, in] layout."""
+    return list(zip(_VISION_ORDER, vision_shapes(h)))
+
+
+def _vision_init(name, shape, rng):
+    """Synthetic values that keep activations O(1): matrices ~N(0, 1/fan_in),
+    biases ~N(0, 0.02^2), norm weights ~1 + N(0, 0.05^2), position table ~N(0, 0.5^2)."""
+    n = int(np.prod(shape))
+    if name.endswith("norm_w") or name in ("norm1_w", "norm2_w"):
+        return 1.0 + 0.05 * rng.standard_normal(n, dtype=np.float32)
+    if name.endswith("_b"):
+        return 0.02 * rng.standard_normal(n, dtype=np.float32)
+    if name == "pos_w":
+        return 0.5 * rng.standard_normal(n, dtype=np.float32)
+    fan_in = shape[-1] if name != "patch_w" else int(np.prod(shape[1:]))
+    return rng.standard_normal(n, dtype=np.float32) / np.float32(np.sqrt(fan_in))
 
 
 def vision_shapes(h: dict):
-    """Shapes of the vision-tower tensors in file order (load_model.cpp:199-246;
-    2304 position embeddings, 3 channels and 3 deep-stack mergers are fixed
-    there)."""
+    """Shapes of the vision-tower tensors in file order (load_model.cpp:199-246)."""
     VH, VD, VI = h["vision_hidden_size"], h["vision_depth"], h["vision_intermediate_size"]
     VP, VTP, OH = h["vision_patch_size"], h["vision_temporal_patch_size"], h["out_hidden_size"]
     VNPE, VC, VDSD = 2304, 3, 3
@@ -194,6 +220,38 @@ def vision_shapes(h: dict):
             (VD, VH), (VD, VH), (VD, VH), (VD, VH),
             (VDSD, VI), (VDSD, VI, VI), (VDSD, OH), (VDSD, OH, VI), (VDSD, VI), (VDSD, VI),
             (VI,), (VI, VI), (OH,), (OH, VI), (VH,), (VH,)]
+
+
+def text_bytes(hdr: dict) -> int:
+    """Bytes of the header plus the text tensors (where the vision tower starts)."""
+    off = HEADER_BYTES
+    for name, shp, _ in _TEXT_ORDER:
+        shape = tuple(int(v) for v in shp(hdr))
+        ns, _ = _scale_count(name, shape, dict(hdr, text_bits=8))
+        off += 4 * ns + int(np.prod(shape))
+    return off
+
+
+def map_vision_tensors(path: str) -> dict:
+    """Host views (memory-mapped, fp16 or fp32 per vision_bits) of the vision
+    tower: name -> array of its shape, in the exporter's [out, in] layout."""
+    hdr = read_header(path)
+    if hdr["text_bits"] != 8:
+        raise ModelFileError("only INT8 text weights are read")
+    dt = {16: np.float16, 32: np.float32}.get(hdr["vision_bits"])
+    if dt is None:
+        raise ModelFileError(f"vision_bits={hdr['vision_bits']}")
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    off = text_bytes(hdr)
+    out = {}
+    es = np.dtype(dt).itemsize
+    for name, shape in vision_tensors(hdr):
+        n = int(np.prod(shape))
+        if off + n * es > mm.size:
+            raise ModelFileError(f"{path}: truncated at vision tensor {name}")
+        out[name] = mm[off:off + n * es].view(dt).reshape(shape)
+        off += n * es
+    return out
 
 
 def synthetic_text(header: dict, seed: int = 0):
