@@ -140,6 +140,7 @@ class RefModel:
             L.refm_free.argtypes = []
             L.refm_forward_img.argtypes = [_P, _I, _I, _I, _P, _P]
             L.refm_forward_img.restype = _I
+            L.refm_set_vision.argtypes = [_P, _P, _I]
             RefModel._libs[so] = L
         L = self._lib = RefModel._libs[so]
         if L.refm_load(path.encode(), int(fp16_kv)) != 0:
@@ -179,6 +180,13 @@ class RefModel:
         if r != d:
             raise RuntimeError("forward_img failed")
         return x, deep
+
+    def set_vision(self, x: np.ndarray, deep: np.ndarray):
+        """Image embeddings [n, out_hidden] and deep-stack rows [3, n, hidden]
+        for the image tokens of the next prompt (in place of forward_img's)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        deep = np.ascontiguousarray(deep, dtype=np.float32)
+        self._lib.refm_set_vision(x.ctypes.data, deep.ctypes.data, x.shape[0])
 
     def close(self):
         self._lib.refm_free()

@@ -178,6 +178,24 @@ int refm_forward_img(const float *patches, int n_patches, int grid_h, int grid_w
     return d_tokens;
 }
 
+// Puts given image embeddings [d_tokens, out_hidden] (fp32) and deep-stack
+// rows [3][d_tokens][hidden] (rounded to the reference's fp16) where
+// forward_img leaves its results, and restarts the image-token counter, so
+// that forward_text on a prompt with image tokens reads them
+// (model/src/forward.cpp:476-485, 665-673).
+void refm_set_vision(const float *x, const float *deep, int d_tokens) {
+    const size_t oh = (size_t)g_cfg.out_hidden_size, H = (size_t)g_cfg.hidden_size;
+    memcpy(g_st.vision_x->ptr(), x, (size_t)d_tokens * oh * sizeof(float));
+    const size_t vnp_max = g_st.vision_deep_stack->shape[1];
+    half_float::half *ds = (half_float::half *)g_st.vision_deep_stack->ptr();
+    for (int d = 0; d < g_cfg.vision_deep_stack_depth; ++d)
+        for (int i = 0; i < d_tokens; ++i)
+            for (size_t j = 0; j < H; ++j)
+                ds[((size_t)d * vnp_max + i) * H + j] = half_float::half(deep[((size_t)d * d_tokens + i) * H + j]);
+    g_st.vision_embed_tokens = d_tokens;
+    g_st.cur_img_token_id = 0;
+}
+
 // Releases the model so that another file can be loaded (the mapped weight
 // files stay mapped: the reference's destructor unmaps an unaligned address).
 void refm_free(void) {

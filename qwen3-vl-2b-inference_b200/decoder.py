@@ -33,6 +33,7 @@ from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Wo
                attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
                qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct)
 from . import load_library
+from . import swiglu as swiglu_
 
 
 @dataclasses.dataclass
@@ -305,15 +306,24 @@ class TextDecoder:
                     inplace_form=True)
         linear_batched(qx, qx_s, [(t["embed"], t["embed_s"])], [self.logits[:B]], ws)
 
-    def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0):
+    def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0, image_embeds=None, deepstack=None,
+                image_token_id: int = 151655, order: str = "tiled"):
         """Prompt of T tokens of request `seq` at positions start..start+T-1 as
-        one M=T pass: every linear is one tensor-core product (the reference's
-        M>1 order), attention is causal over the paged cache (query t sees
+        one M=T pass, attention causal over the paged cache (query t sees
         positions <= start+t).  Leaves the last token's logits and greedy id in
         self.logits[seq] / self.tokens[seq] and self.positions[seq] = start+T.
-        The reference has no batched prefill: it feeds the prompt one token at
-        a time (model/src/utils.cpp:143-160); per token the arithmetic is the
-        same up to the GEMM order."""
+
+        order "tiled": every linear is one tensor-core product (the reference's
+        M>1 order).  order "lane8": every row in the reference's M=1 order and
+        attention in its summation order (with attn_order "reference"), i.e.
+        exactly what the reference computes when it feeds the prompt one token
+        at a time (model/src/utils.cpp:143-160).
+
+        image_embeds fp32 [n, H] / deepstack fp16 [3, n, H] (the vision tower's
+        outputs): the k-th prompt token equal to image_token_id takes row k of
+        image_embeds instead of its embedding, and after layers 0..2 row k of
+        deepstack[l] is added to it (forward_text, model/src/forward.cpp:476-485,
+        665-673)."""
         cfg, t = self.cfg, self.w.t
         T = tokens.numel()
         H, I, D, ng, eps = cfg.hidden, cfg.intermediate, cfg.head_dim, cfg.norm_group, cfg.eps
@@ -340,20 +350,36 @@ class TextDecoder:
         sq, ps = pf["seq"][:T], pf["pos"][:T]
         ws = pf["ws"]
         embedding_lookup_i8(t["embed"], t["embed_s"], tokens.to(torch.int32), x)
-        prod = self._prefill_product
+        img_rows = None
+        if image_embeds is not None:
+            img_rows = torch.nonzero(tokens.reshape(-1) == image_token_id).reshape(-1)
+            n_img = img_rows.numel()
+            if n_img > image_embeds.shape[0]:
+                raise ValueError(f"{n_img} image tokens, {image_embeds.shape[0]} image embeddings")
+            x[img_rows] = image_embeds[:n_img].to(torch.float32)
+        lane8 = order == "lane8"
+        if order not in ("tiled", "lane8"):
+            raise ValueError(order)
+        prod = self._prefill_product_lane8 if lane8 else self._prefill_product
+        attn = attention_ordered if self.attn_order == "reference" else attention
+        if self.attn_order == "reference":
+            ws.get(load_library().qvl_attention_ordered_workspace_bytes(T, self.max_ctx, self.kv[0].dims))
         for l in range(cfg.layers):
             rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
             prod(qh, qs, ("wq", "wk", "wv"), l, [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
             qknorm_rope_kv_append(pf["q"][:T], pf["k"][:T], pf["v"][:T], self.kv[l], sq, ps, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
-            attention(pf["q"][:T], self.kv[l], sq, ps, self.max_ctx, out=pf["att"][:T], workspace=ws)
+            attn(pf["q"][:T], self.kv[l], sq, ps, self.max_ctx, out=pf["att"][:T], workspace=ws)
             _quantize_into(pf["att"][:T], qh, qs)
             prod(qh, qs, ("wo",), l, [x], ws, acc=True)
             rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
             prod(qh, qs, ("wg", "wu"), l, [pf["gate"][:T], pf["up"][:T]], ws, swiglu=True, up_scratch=pf["up"][:T])
             _quantize_into(pf["gate"][:T], q16, qs)
             prod(q16, qs, ("wd",), l, [x], ws, acc=True)
+            if img_rows is not None and l < deepstack.shape[0]:
+                # add_vector(x, deep-stack row): fp32 x + the fp16 value
+                x[img_rows] += deepstack[l, :img_rows.numel()].to(torch.float32)
         last = x[T - 1:T]
         rms_norm_i8(last, t["final_norm"], t["final_norm_s"], ng, eps, out=last, q=qh[:1], q_scales=qs[:1],
                     quant_group=H, inplace_form=True)
@@ -388,6 +414,17 @@ class TextDecoder:
         if b is None or b.numel() < int(np.prod(shape)):
             b = bufs[key] = torch.empty(int(np.prod(shape)), dtype=dtype, device=self.device)
         return b[:int(np.prod(shape))].view(shape)
+
+    def _prefill_product_lane8(self, q, qs, names, l, outs, ws, acc=False, swiglu=False, up_scratch=None):
+        """The products of the prompt rows in the reference's M=1 order (each
+        row as its own GEMV), then swiglu(gate, up) into gate."""
+        t = self.w.t
+        K = q.shape[1]
+        for n, out in zip(names, outs):
+            linear_q16(q, qs, t[n][l], t[n + "_s"][l], K, C=out,
+                       semantics=SEM_LANE8 | (SEM_ACCUMULATE if acc else 0))
+        if swiglu:
+            swiglu_(outs[0], outs[1])
 
     def _prefill_product(self, q, qs, names, l, outs, ws, acc=False, swiglu=False, up_scratch=None):
         """outs[i] (+)= q . dequant(W_names[i])^T for the prompt rows, one
