@@ -706,6 +706,72 @@ def run_decode_batch(w, B, args, dev):
     return out
 
 
+def run_config4(w, args, dev):
+    """BASELINE config 4, one request end to end on this GPU: a synthetic
+    448x448 image (host patches, pinned) and 256 text ids go to the device,
+    the vision tower runs (784 patches -> 196 image tokens + deep stack),
+    the 454-token prompt pass (tensor-core products, image embeddings and
+    deep-stack rows in place), then N greedy tokens (one launch each), and
+    the ids come back to the host.  Synthetic weights (text: the bench's
+    decoder weights; vision: random fp16)."""
+    import numpy as np
+    import torch
+    import qvl_b200.decoder as D
+    import qvl_b200.modelfile as MF
+    import qvl_b200.vision as V
+    n_new = args.config4_tokens
+    hdr = MF.qwen3vl_2b_header()
+    rng = np.random.default_rng(4)
+    img = rng.integers(0, 256, (448, 448, 3), dtype=np.uint8)
+    patches, gh, gw = V.image_patches(img)
+    enc = V.VisionEncoder.random(hdr, gh, gw, device=dev, seed=4)
+    n_img = enc.D
+    prompt = ([hdr["vision_start_token_id"]] + [hdr["image_token_id"]] * n_img + [hdr["vision_end_token_id"]] +
+              rng.integers(0, 151643, 256).tolist())
+    T = len(prompt)
+    dec = D.TextDecoder(w, max_batch=1, max_ctx=T + n_new + 8, device=dev, persistent=True,
+                        attn_order=args.attn_order)
+    patches_h = torch.from_numpy(patches).pin_memory()
+    prompt_h = torch.tensor(prompt, dtype=torch.int32).pin_memory()
+    patches_d = torch.empty(patches.shape, dtype=torch.float32, device=dev)
+    prompt_d = torch.empty(T, dtype=torch.int32, device=dev)
+    ids_d = torch.empty(n_new, dtype=torch.int32, device=dev)
+    ids_h = torch.empty(n_new, dtype=torch.int32).pin_memory()
+    stream = torch.cuda.Stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+
+    def request():
+        with torch.cuda.stream(stream):
+            ev[0].record(stream)
+            patches_d.copy_(patches_h, non_blocking=True)
+            prompt_d.copy_(prompt_h, non_blocking=True)
+            emb, deep = enc.forward(patches_d)
+            ev[1].record(stream)
+            dec.prefill(prompt_d, image_embeds=emb, deepstack=deep)
+            ev[2].record(stream)
+            for i in range(n_new):
+                dec.step()
+                ids_d[i:i + 1].copy_(dec.tokens[:1])
+            ev[3].record(stream)
+            ids_h.copy_(ids_d, non_blocking=True)
+            ev[4].record(stream)
+        stream.synchronize()
+
+    request()                                    # warm-up (kernel set-up, workspaces)
+    t0 = time.perf_counter()
+    request()
+    wall = time.perf_counter() - t0
+    out = {"workload": "config4: 448x448 image (196 image tokens) + 256 text ids -> "
+                       f"{n_new} greedy tokens, batch 1, one request",
+           "request_s": round(wall, 4), "generated_tokens_per_s": round(n_new / wall, 1),
+           "vision_ms": round(ev[0].elapsed_time(ev[1]), 3), "prefill_ms": round(ev[1].elapsed_time(ev[2]), 3),
+           "decode_tokens_per_s": round(n_new / (ev[2].elapsed_time(ev[3]) / 1e3), 1),
+           "prompt_tokens": T, "h2d_bytes": int(patches.nbytes + 4 * T), "d2h_bytes": 4 * n_new}
+    del dec, enc
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -825,9 +891,12 @@ def run_ours(args):
         if aborted:
             raise RuntimeError("persistent decode: a grid barrier wait timed out")
     batch32 = None
+    config4 = None
     if rank == 0 and args.batch == 1 and args.batch32_steps > 0:
         del g, ge
         batch32 = run_decode_batch(w, 32, args, dev)
+    if rank == 0 and args.batch == 1 and args.config4_tokens > 0:
+        config4 = run_config4(w, args, dev)
     gemv0 = run_gemv(dev) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = load_peaks()
@@ -879,6 +948,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gemv_config0": gemv0,
             "batch32": batch32,
+            "config4": config4,
         }))
     if ws > 1:
         dist.destroy_process_group()
@@ -898,6 +968,8 @@ def main():
                     help="decode attention: the reference's summation order (bit-identical logits) or split context")
     ap.add_argument("--tp", action="store_true",
                     help="prefill: split every product of one prompt by output column over the ranks")
+    ap.add_argument("--config4-tokens", type=int, default=128,
+                    help="greedy tokens of the config-4 request in the bench line (0: skip)")
     ap.add_argument("--batch32-steps", type=int, default=32, help="steps of the batch-32 figure (0: skip)")
     ap.add_argument("--engine", default="auto", choices=["auto", "persistent", "chain"],
                     help="decode: one cooperative launch per token (batch 1) or the per-operator launch chain")

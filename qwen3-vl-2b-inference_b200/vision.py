@@ -78,8 +78,43 @@ def image_patches(rgb: np.ndarray, patch: int = 16, merge: int = 2, temporal: in
 class VisionEncoder:
     """forward_img on the GPU for images of one grid size."""
 
-    def __init__(self, path: str, grid_h: int, grid_w: int, device="cuda"):
-        h = read_header(path)
+    @classmethod
+    def from_file(cls, path: str, grid_h: int, grid_w: int, device="cuda"):
+        """Weights from a model file's vision tower (vision_bits 16)."""
+        vt = map_vision_tensors(path)
+        if vt["patch_w"].dtype != np.float16:
+            raise ValueError("vision_bits must be 16")
+        dev = torch.device(device)
+        return cls(read_header(path), {k: torch.from_numpy(np.array(v, copy=True)).to(dev) for k, v in vt.items()},
+                   grid_h, grid_w, device)
+
+    @classmethod
+    def random(cls, header: dict, grid_h: int, grid_w: int, device="cuda", seed: int = 0):
+        """Synthetic fp16 weights at the header's sizes, drawn on the device
+        with the model-file writer's scales (no checkpoint is available)."""
+        from .modelfile import vision_tensors
+        dev = torch.device(device)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        t = {}
+        for name, shape in vision_tensors(header):
+            r = torch.randn(shape, generator=g, device=dev)
+            if name in ("norm1_w", "norm2_w") or name.endswith("norm_w"):
+                r = 1.0 + 0.05 * r
+            elif name.endswith("_b"):
+                r = 0.02 * r
+            elif name == "pos_w":
+                r = 0.5 * r
+            else:
+                fan_in = shape[-1] if name != "patch_w" else int(np.prod(shape[1:]))
+                r = r / float(np.sqrt(fan_in))
+            t[name] = r.half()
+        return cls(header, t, grid_h, grid_w, device)
+
+    def __init__(self, header: dict, tensors: dict, grid_h: int, grid_w: int, device="cuda"):
+        """header: the model file's header values; tensors: name -> fp16
+        device tensor of the vision tower (modelfile.vision_tensors names and
+        shapes, [out, in] layout)."""
+        h = header
         self.h = h
         self.dev = dev = torch.device(device)
         self.VH, self.VI, self.OH = h["vision_hidden_size"], h["vision_intermediate_size"], h["out_hidden_size"]
@@ -93,10 +128,7 @@ class VisionEncoder:
         self.D = self.T // (self.merge * self.merge)
         if self.merge * self.merge * self.VH != self.VI:
             raise ValueError("the deep-stack and merger layers take merge^2 * vision_hidden = vision_intermediate")
-        vt = map_vision_tensors(path)
-        if vt["patch_w"].dtype != np.float16:
-            raise ValueError("vision_bits must be 16")
-        self.w = {k: torch.from_numpy(np.array(v, copy=True)).to(dev) for k, v in vt.items()}
+        self.w = dict(tensors)
         self.w["patch_w"] = self.w["patch_w"].reshape(self.VH, -1)
         L = _lib()
         T, HD = self.T, self.HD

@@ -32,7 +32,7 @@ def test_config4_image_prompt_then_greedy_decode(qvl, cuda, tmp_path):
     rng = np.random.default_rng(12)
     img = rng.integers(0, 256, (448, 448, 3), dtype=np.uint8)
     patches, gh, gw = V.image_patches(img)
-    enc = V.VisionEncoder(path, gh, gw, device=cuda)
+    enc = V.VisionEncoder.from_file(path, gh, gw, device=cuda)
     emb, deep = enc.forward(torch.from_numpy(patches).to(cuda))
     n_img = emb.shape[0]
     assert n_img == 196

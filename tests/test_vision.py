@@ -103,7 +103,7 @@ def test_vision_tower_matches_reference_forward_img(qvl, cuda, tmp_path):
     MF.write_model_bin(path, hdr, MF.synthetic_text(hdr, seed=1), rng=np.random.default_rng(7))
     img = np.random.default_rng(0).integers(0, 256, (448, 448, 3), dtype=np.uint8)
     patches, gh, gw = V.image_patches(img)
-    enc = V.VisionEncoder(path, gh, gw, device=cuda)
+    enc = V.VisionEncoder.from_file(path, gh, gw, device=cuda)
     out, deep = enc.forward(torch.from_numpy(patches).to(cuda))
     torch.cuda.synchronize()
     rm = oracle.RefModel(path)
