@@ -173,8 +173,8 @@ def run_reference(args):
     if rank != 0:
         return
     import oracle
-    if not oracle.ref_available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqwen_ref.so not built"}))
+    if not (oracle.ref_available() or oracle.ref_model_available()):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference compiled from its sources) not built"}))
         return
     tps, n, dt = cpu_decode_rate(args, seconds=None, steps=args.steps, warmup=args.warmup)
     print(json.dumps({
@@ -183,7 +183,8 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32",
         "data": "synthetic (random-init int8 weights, seed 0)", "config": decode_config(args, 1),
         "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
-                         "sample": f"{n} decode tokens, batch 1 (reference runs one request at a time)"},
+                         "sample": f"{n} decode tokens, batch 1 (the reference runs one request at a time): its own "
+                                   f"init_model_weights + forward_text on a synthetic model file"},
         "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -201,11 +202,55 @@ def decode_config(args, ws):
 _cpu_state = {}
 
 
+def _ref_model_file():
+    """A synthetic model file in the exporter's layout (full-size text
+    decoder, per-row INT8; a minimal vision tower, which forward_text does not
+    touch) for the reference's own loader; written once per process."""
+    path = _cpu_state.get("bin")
+    if path is None:
+        import tempfile
+        import_qvl()
+        import qvl_b200.modelfile as MF
+        hdr = MF.qwen3vl_2b_header(vision_hidden_size=32, vision_intermediate_size=64, vision_num_heads=2)
+        import atexit
+        import shutil
+        d = tempfile.mkdtemp(prefix="qvl_bench_")
+        atexit.register(shutil.rmtree, d, True)
+        path = os.path.join(d, "qwen3vl2b_text_rowwise.bin")
+        MF.write_model_bin(path, hdr, MF.synthetic_text(hdr, seed=0))
+        _cpu_state["bin"] = path
+    return path
+
+
 def cpu_decode_rate(args, seconds=None, steps=None, warmup=2):
-    """Reference CPU decode (compiled reference operators, all host cores) on
-    the same synthetic model; bounded by `seconds` or `steps`."""
+    """Reference CPU decode on the same model shape, all host cores, bounded by
+    `seconds` or `steps`: the reference's own loader and forward_text
+    (oracle.RefModel, its FP32 KV cache) when that library is built, else its
+    compiled operators composed in forward_text order (oracle/decode.py)."""
     import torch
     import oracle
+    if oracle.ref_model_available():
+        rm = oracle.RefModel(_ref_model_file(), fp16_kv=False)
+        try:
+            rng = np.random.default_rng(0)
+            rm.k_cache[:, :, :PROMPT_CTX] = rng.standard_normal(rm.k_cache[:, :, :PROMPT_CTX].shape, dtype=np.float32)
+            rm.v_cache[:, :, :PROMPT_CTX] = rng.standard_normal(rm.v_cache[:, :, :PROMPT_CTX].shape, dtype=np.float32)
+            tok, pos = 5, PROMPT_CTX
+            for _ in range(warmup):
+                tok = oracle.argmax(rm.forward(tok, pos))
+                pos += 1
+            n, t0 = 0, time.perf_counter()
+            while True:
+                tok = oracle.argmax(rm.forward(tok, pos))
+                pos += 1
+                n += 1
+                el = time.perf_counter() - t0
+                if (steps is not None and n >= steps) or (seconds is not None and el >= seconds):
+                    break
+        finally:
+            rm.close()
+        dt = el / n
+        return 1.0 / dt, n, dt
     from oracle.decode import CpuDecoder
     import_qvl()
     import qvl_b200.decoder as D
@@ -924,8 +969,9 @@ def run_ours(args):
             import oracle
             cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": os.cpu_count(),
                    "kind": "reference" if oracle.ref_available() else "port",
-                   "sample": f"{n} decode tokens of one request ({dt * 1e3:.1f} ms each), same model shape, "
-                             f"reference operators compiled from its sources, OpenMP on all cores"}
+                   "sample": f"{n} decode tokens of one request ({dt * 1e3:.1f} ms each), same model shape: "
+                             f"the reference's own loader + forward_text compiled from its sources (FP32 KV), "
+                             f"OpenMP on all cores"}
         print(json.dumps({
             "metric": "decode_tokens_per_s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,

@@ -578,6 +578,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 S.v_pages[off + j] = __half_as_ushort(__float2half_rn(__ldcg(S.qkv + NH * D + NKV * D + kvh * D + j)));
             }
             csync();                 // the appended key row is read back below
+            if (l == 5) DETAIL(250);
             float qv[2][8];
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -675,7 +676,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 1; w < kPWarps; ++w) m = fmaxf(m, redf[threadIdx.x][w]);
                 S.att_lmax[(kvh * 2 + threadIdx.x) * kSlices + sl] = m;
             }
+            if (l == 5) DETAIL(251);
             if (!head_sync(S, kvh)) { drain(); return; }
+            if (l == 5) DETAIL(252);
         }
 
         // ---- attention, phase 2: probabilities (global max), slice sum, partial P.V
@@ -717,7 +720,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 // element is one fma chain over t ascending.  E and this CTA's
                 // 16-byte column of V are staged in shared memory (xs) 1024
                 // positions at a time.
+                if (l == 5) DETAIL(253);
                 if (!head_sync(S, kvh)) { drain(); return; }
+                if (l == 5) DETAIL(254);
                 constexpr int kCh = 1024;
                 float *ebuf = xs;                                   // [2][kCh]
                 uint4 *vbuf = reinterpret_cast<uint4 *>(xs + 2 * kCh);   // [kCh] 8 halves each
@@ -784,6 +789,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                     if (!one) csync();
                 }
                 if (threadIdx.x < 16) S.att_out[(kvh * 2 + h) * D + d0 + j] = scratch[32 + h] != 0.0f ? a : 0.0f;
+                if (l == 5) DETAIL(255);
             } else {
             float acc[2][8];
 #pragma unroll
@@ -931,6 +937,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(S.h) + i);
         csync();
         quantize_row_n<I>(xs, q16, &a_s_sh, scratch);
+        if (l == 5) DETAIL(234);
         {
             const int nu = cta_units(ph_units(PH_DOWN, W.vocab));
             for (int j = 0; j < nu; ++j) {
@@ -949,6 +956,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 if (lane == 0) S.x[n] = add_rn(xn, out);
             }
         }
+        if (l == 5) DETAIL(235);
         GRID_ARRIVE();
         if (l + 1 < W.layers) stage_norm(W.in_norm + (size_t)(l + 1) * H, W.in_norm_s + (size_t)(l + 1) * (H / ng));
         else stage_norm(W.final_norm, W.final_norm_s);
