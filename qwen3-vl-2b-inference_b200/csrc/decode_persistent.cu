@@ -48,6 +48,7 @@ constexpr int kPWarps = ring::kWarps;
 constexpr int H = 2048, I = 6144, NH = 16, NKV = 8, D = 128;
 constexpr int kSlices = kPersistSlices;        // attention context slices per KV head
 constexpr int kSliceMax = 512;                 // tokens per slice (context <= 8192)
+constexpr int kOrdChunk = 1024;               // positions staged per pass in reference-order attention
 constexpr int kMaxPages = kSlices * kSliceMax / 16;   // page table entries (page_size >= 16)
 constexpr unsigned long long kBarrierLimitNs = 2000000000ull;
 constexpr unsigned kTraceSlots = kPersistTraceSlots;
@@ -81,20 +82,24 @@ __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
 }
 // Grid barrier with a bounded wait.  The counter only grows (it is zero
 // when the workspace is cleared), so barrier k of a launch completes when
-// the arrivals reach the next multiple of gridDim.x: no reset, no second
-// word.  Release on arrival / acquire on the wait, each after / before a CTA
+// the arrivals reach base + (k + 1) * gridDim.x, base being the counter at
+// kernel entry rounded down to a multiple of gridDim.x: no reset, no second
+// word, and the arrival is a fire-and-forget reduction (no reply to wait
+// for).  Release on arrival / acquire on the wait, each after / before a CTA
 // barrier (the CTA's writes are ordered by bar.sync, then published by the
 // release).  Returns false if the wait gave up or another CTA aborted.
 // CTA 0 records the time each barrier opens in S.trace[1 + k].
 // Barrier of the kSlices CTAs of one KV head (the softmax needs the maximum
 // over the head's slices only); same counter scheme as the grid barrier.
-__device__ __forceinline__ bool head_sync(const PersistState &S, int kvh) {
+__device__ __forceinline__ bool head_sync(const PersistState &S, int kvh, unsigned long long &target) {
     csync();
     __shared__ int ok;
     if (threadIdx.x == 0) {
-        unsigned long long old, v;
-        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.head_bar + kvh) : "memory");
-        const unsigned long long target = (old / kSlices + 1) * kSlices;
+        // arrive without waiting for the atomic's reply: the target is known
+        // (this CTA's count of head barriers so far, from the base read at entry)
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(S.head_bar + kvh) : "memory");
+        target += kSlices;
+        unsigned long long v;
         int good = 1;
         const unsigned long long t0 = global_ns();
         for (unsigned it = 1;; ++it) {
@@ -120,9 +125,10 @@ __device__ __forceinline__ bool head_sync(const PersistState &S, int kvh) {
 __device__ __forceinline__ void grid_arrive(const PersistState &S, unsigned long long &target) {
     csync();
     if (threadIdx.x == 0) {
-        unsigned long long old;
-        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(S.bar_count) : "memory");
-        target = (old / gridDim.x + 1) * gridDim.x;
+        // no reply needed: the completing count is this CTA's previous target
+        // plus the grid size (the base was read at kernel entry)
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(S.bar_count) : "memory");
+        target += gridDim.x;
     }
 }
 __device__ __forceinline__ bool grid_wait(const PersistState &S, unsigned long long target, int &nsync) {
@@ -334,6 +340,12 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     const int4 *q_s = reinterpret_cast<const int4 *>(q16);
     float *nrm_w = sp + 2 * kSliceMax;     // [H] next RMSNorm weight (dequantised int8 value)
     float *nrm_s = nrm_w + H;               // [H / norm_group] its group scales
+    // reference-order attention, phase 2 (q16 | xs | ts are free then):
+    // exponentials [2][kOrdChunk] f32, V rows [kOrdChunk] x 8 halves, and the
+    // same V transposed [8][kOrdChunk] halves -- 40 KB of the 44 KB region
+    float *ord_e = reinterpret_cast<float *>(q16);
+    uint4 *ord_v = reinterpret_cast<uint4 *>(ord_e + 2 * kOrdChunk);
+    __half *ord_vt = reinterpret_cast<__half *>(ord_e + 6 * kOrdChunk);
     __shared__ __align__(8) uint64_t full_mb[kStages];
     __shared__ __align__(16) float ring_scales[kStages][kRows];   // per-row weight scales of each stage
     __shared__ __align__(8) uint64_t empty_mb[kStages];
@@ -354,6 +366,8 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     const uint32_t ring = tc::smem_u32(ring_ptr);
     const uint32_t full_bar = tc::smem_u32(full_mb), empty_bar = tc::smem_u32(empty_mb);
     const uint32_t ring_s = tc::smem_u32(&ring_scales[0][0]);
+    unsigned long long bar_target = 0;  // thread 0: count that completes the current grid barrier
+    unsigned long long head_target = 0; // thread 0: count that completes the current head barrier
     Producer prod;                      // used by the producer lane only
     int cons = 0;                       // stages consumed (same count in every compute thread)
     int nsync = 0;                      // grid barriers passed
@@ -365,6 +379,18 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         // vocabulary, decodes nothing either: every CTA sees the same values,
         // so all leave before any load that depends on them, and the word
         // tells the host why (token and pos are left unchanged).
+        // barrier counters are monotonic across launches and complete at
+        // multiples of their participant counts; no barrier of this launch can
+        // complete before this CTA arrives, so rounding down gives the base
+        {
+            unsigned long long v;
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.bar_count) : "memory");
+            bar_target = (v / gridDim.x) * gridDim.x;
+            if (blockIdx.x < NKV * kSlices) {
+                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(S.head_bar + blockIdx.x / kSlices) : "memory");
+                head_target = (v / kSlices) * kSlices;
+            }
+        }
         const int p0 = S.pos[0], t0 = S.token[0];
         if (!aborted_at_entry && (p0 < 0 || p0 >= S.max_ctx || t0 < 0 || t0 >= W.vocab)) {
             aborted_at_entry = 1;
@@ -407,10 +433,11 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
     };
 #ifdef QVL_PERSIST_DETAIL
 #define DETAIL(slot) do { if (blockIdx.x == 0 && threadIdx.x == 0) S.trace[slot] = global_ns(); } while (0)
+#define DETAIL_ALL(slot) do { if (threadIdx.x == 0) S.trace[(slot) + blockIdx.x] = global_ns(); } while (0)
 #else
 #define DETAIL(slot) do { } while (0)
+#define DETAIL_ALL(slot) do { } while (0)
 #endif
-    unsigned long long bar_target = 0;       // thread 0: arrivals that complete the current barrier
 #define GRID_ARRIVE() grid_arrive(S, bar_target)
 #define GRID_WAIT_OR_EXIT()                                                               \
     do {                                                                                  \
@@ -630,6 +657,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                         }
                         const float sc = mul_rn(r, inv_sqrt_d);
                         sp[h * kSliceMax + t] = sc;
+                        __stcg(S.att_e + (size_t)(kvh * 2 + h) * (kSlices * kSliceMax) + t0 + t, sc);
                         if (h == 0) mx[0] = fmaxf(mx[0], sc); else mx[1] = fmaxf(mx[1], sc);
                     }
                     csync();
@@ -676,29 +704,182 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 1; w < kPWarps; ++w) m = fmaxf(m, redf[threadIdx.x][w]);
                 S.att_lmax[(kvh * 2 + threadIdx.x) * kSlices + sl] = m;
             }
+            if (S.ordered && ctx <= kOrdChunk) {
+                // this slice CTA's output columns [8*sl, 8*sl+8) of V at every
+                // cached position, fetched while the head barrier completes;
+                // the new position's row (appended by its owner slice in this
+                // phase) is read after the barrier
+                csync();            // the key staging area (xs) is free
+                const uint32_t vb = tc::smem_u32(ord_v);
+                for (int t = threadIdx.x; t < ctx - 1; t += kPThreads)
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(vb + 16u * (uint32_t)t),
+                                 "l"(S.v_pages + kv_off(S, pt_sm, l, t, kvh) + 8 * sl)
+                                 : "memory");
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            }
             if (l == 5) DETAIL(251);
-            if (!head_sync(S, kvh)) { drain(); return; }
+            if (!head_sync(S, kvh, head_target)) { drain(); return; }
             if (l == 5) DETAIL(252);
         }
 
         // ---- attention, phase 2: probabilities (global max), slice sum, partial P.V
         if (attn_cta) {
             __shared__ float gm[2];
+            // reference order, one chunk: this thread's scores (2 per thread
+            // at ctx <= 512, 4 at 1024) load while the maxima are combined
+            float pre[4];
+            const bool pre_ok = S.ordered && ctx <= kOrdChunk && 2 * ctx <= 4 * kPThreads;
+            if (pre_ok) {
+                const float *s0 = S.att_e + (size_t)(kvh * 2) * (kSlices * kSliceMax);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = threadIdx.x + u * kPThreads;
+                    const int h = e >= ctx, k = h ? e - ctx : e;
+                    pre[u] = e < 2 * ctx ? __ldcg(s0 + (size_t)h * (kSlices * kSliceMax) + k) : 0.0f;
+                }
+            }
             if (threadIdx.x < 2) {
                 float m = -INFINITY;
                 for (int s2 = 0; s2 < kSlices; ++s2) m = fmaxf(m, __ldcg(S.att_lmax + (kvh * 2 + threadIdx.x) * kSlices + s2));
                 gm[threadIdx.x] = m;
             }
             csync();
+            if (l == 5) DETAIL(256);
+            if (S.ordered) {
+                // reference order (layers/src/text_layer.cpp:473-535, 677-689).
+                // Every slice CTA reads all of the head's scores (written to the
+                // workspace in phase 1) and forms the exponentials with the
+                // global maximum itself, so no second barrier is needed; it then
+                // sums them into 8 float lanes t-ascending, the lanes then the
+                // tail in double, and runs the fma chains (one per output
+                // element, t ascending) of its 8 output dimensions of both
+                // query heads, p = e * (float)(1/sum).  The exponentials and the
+                // V column are staged in shared memory, kOrdChunk positions at
+                // a time (V already fetched during the head barrier when the
+                // context fits one chunk).
+                constexpr int kCh = kOrdChunk;
+                float *ebuf = ord_e;                                // [2][kCh]
+                uint4 *vbuf = ord_v;                                // [kCh] 8 halves each
+                const int d0 = 8 * sl, n8 = (ctx / 8) * 8;
+                const float *s0 = S.att_e + (size_t)(kvh * 2) * (kSlices * kSliceMax);
+                const float *s1 = s0 + kSlices * kSliceMax;
+                const bool one = ctx <= kCh;
+                auto stage = [&](int c0, int n, bool with_v) {
+                    if (pre_ok) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int e = threadIdx.x + u * kPThreads;
+                            if (e < 2 * n) {
+                                const int h = e >= n, k = h ? e - n : e;
+                                ebuf[h * kCh + k] = (pre[u] > -INFINITY) ? exp_ref(pre[u] - gm[h]) : 0.0f;
+                            }
+                        }
+                    } else {
+                        for (int e = threadIdx.x; e < 2 * n; e += kPThreads) {
+                            const int h = e >= n, k = h ? e - n : e;
+                            const float sv = __ldcg((h ? s1 : s0) + c0 + k);
+                            ebuf[h * kCh + k] = (sv > -INFINITY) ? exp_ref(sv - gm[h]) : 0.0f;
+                        }
+                    }
+                    if (with_v)
+                        for (int e = threadIdx.x; e < n; e += kPThreads)
+                            vbuf[e] = __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, pt_sm, l, c0 + e, kvh) + d0));
+                    csync();
+                };
+                float lane_acc = 0.0f;             // thread h*8+ln: lane ln of head h
+                if (one && threadIdx.x == kPThreads - 1)    // the new position's row (see phase 1)
+                    vbuf[ctx - 1] = __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, pt_sm, l, ctx - 1, kvh) + d0));
+                for (int c0 = 0; c0 < ctx; c0 += kCh) {
+                    const int n = min(kCh, ctx - c0);
+                    stage(c0, n, false);
+                    if (threadIdx.x < 16) {
+                        const float *eb = ebuf + (threadIdx.x >> 3) * kCh;
+                        const int ln = threadIdx.x & 7;
+                        // t = c0 + k with t = ln mod 8 (c0 is a multiple of 8), t < n8
+                        const int kend = min(n, n8 - c0);
+                        int k = ln;
+                        for (; k + 56 < kend; k += 64) {        // 8 loads ahead of the serial adds
+                            float e8[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) e8[u] = eb[k + 8 * u];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) lane_acc = add_rn(lane_acc, e8[u]);
+                        }
+                        for (; k < kend; k += 8) lane_acc = add_rn(lane_acc, eb[k]);
+                    }
+                    if (!one) csync();
+                }
+                if (l == 5) DETAIL(257);
+                if (threadIdx.x < 16) scratch[threadIdx.x] = lane_acc;
+                csync();
+                if (l == 5) DETAIL(258);
+                if (threadIdx.x < 2) {
+                    // the tail (at most 7 positions), still staged when one chunk
+                    const int h = threadIdx.x;
+                    double sum = 0.0;
+                    for (int ln = 0; ln < 8; ++ln) sum = __dadd_rn(sum, (double)scratch[h * 8 + ln]);
+                    for (int t = n8; t < ctx; ++t) {
+                        const float sv = one ? 0.0f : __ldcg((h ? s1 : s0) + t);
+                        const float e = one ? ebuf[h * kCh + t] : ((sv > -INFINITY) ? exp_ref(sv - gm[h]) : 0.0f);
+                        sum = __dadd_rn(sum, (double)e);
+                    }
+                    const bool zero = !isfinite(gm[h]) || !(sum > 0.0) || !isfinite(sum);
+                    scratch[32 + h] = zero ? 0.0f : 1.0f;
+                    scratch[34 + h] = __double2float_rn(__ddiv_rn(1.0, sum));
+                }
+                if (one) asm volatile("cp.async.wait_group 0;" ::: "memory");
+                csync();
+                if (l == 5) DETAIL(259);
+                const int h = threadIdx.x >> 3, j = threadIdx.x & 7;
+                float a = 0.0f;
+                for (int c0 = 0; c0 < ctx; c0 += kCh) {
+                    const int n = min(kCh, ctx - c0);
+                    if (!one) stage(c0, n, true);
+                    // p = e * (float)(1/sum) in place, and V transposed to
+                    // [d][t] so that a chain reads 8 positions per 16-byte load
+                    for (int e = threadIdx.x; e < 2 * n; e += kPThreads) {
+                        const int hh = e >= n, k = hh ? e - n : e;
+                        ebuf[hh * kCh + k] = mul_rn(ebuf[hh * kCh + k], scratch[34 + hh]);
+                    }
+                    for (int e = threadIdx.x; e < n; e += kPThreads) {
+                        const uint4 r = vbuf[e];
+                        const __half *hv = reinterpret_cast<const __half *>(&r);
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) ord_vt[jj * kCh + e] = hv[jj];
+                    }
+                    csync();
+                    if (threadIdx.x < 16) {
+                        const float4 *pb = reinterpret_cast<const float4 *>(ebuf + h * kCh);
+                        const uint4 *vt = reinterpret_cast<const uint4 *>(ord_vt + j * kCh);
+                        const int n8c = n & ~7;
+                        for (int k = 0; k < n8c; k += 8) {
+                            const float4 p0 = pb[k / 4], p1 = pb[k / 4 + 1];
+                            const uint4 vr = vt[k / 8];
+                            float vf[8];
+                            h8f(vr, vf);
+                            a = fma_rn(p0.x, vf[0], a);
+                            a = fma_rn(p0.y, vf[1], a);
+                            a = fma_rn(p0.z, vf[2], a);
+                            a = fma_rn(p0.w, vf[3], a);
+                            a = fma_rn(p1.x, vf[4], a);
+                            a = fma_rn(p1.y, vf[5], a);
+                            a = fma_rn(p1.z, vf[6], a);
+                            a = fma_rn(p1.w, vf[7], a);
+                        }
+                        for (int k = n8c; k < n; ++k) a = fma_rn(ebuf[h * kCh + k], __half2float(ord_vt[j * kCh + k]), a);
+                    }
+                    if (!one) csync();
+                }
+                if (threadIdx.x < 16) S.att_out[(kvh * 2 + h) * D + d0 + j] = scratch[32 + h] != 0.0f ? a : 0.0f;
+                if (l == 5) DETAIL(255);
+            } else {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 double part = 0.0;
-                float *eh = S.att_e + (size_t)(kvh * 2 + h) * (kSlices * kSliceMax) + t0;
                 for (int t = threadIdx.x; t < len; t += kPThreads) {
                     const float sv = sp[h * kSliceMax + t];
                     const float p = (sv > -INFINITY) ? exp_ref(sv - gm[h]) : 0.0f;
                     sp[h * kSliceMax + t] = p;
-                    if (S.ordered) __stcg(eh + t, p);
                     part += (double)p;
                 }
 #pragma unroll
@@ -711,86 +892,6 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
                 for (int w = 0; w < kPWarps; ++w) sum += redd[threadIdx.x][w];
                 S.att_lsum[(kvh * 2 + threadIdx.x) * kSlices + sl] = sum;
             }
-            if (S.ordered) {
-                // reference order (layers/src/text_layer.cpp:473-535, 677-689):
-                // once every slice's exponentials are out, each slice CTA takes
-                // 8 output dimensions of both query heads.  The exponentials
-                // are summed into 8 float lanes t-ascending, the lanes then the
-                // tail in double, p = e * (float)(1/sum), and each output
-                // element is one fma chain over t ascending.  E and this CTA's
-                // 16-byte column of V are staged in shared memory (xs) 1024
-                // positions at a time.
-                if (l == 5) DETAIL(253);
-                if (!head_sync(S, kvh)) { drain(); return; }
-                if (l == 5) DETAIL(254);
-                constexpr int kCh = 1024;
-                float *ebuf = xs;                                   // [2][kCh]
-                uint4 *vbuf = reinterpret_cast<uint4 *>(xs + 2 * kCh);   // [kCh] 8 halves each
-                const int d0 = 8 * sl, n8 = (ctx / 8) * 8;
-                const float *e0 = S.att_e + (size_t)(kvh * 2) * (kSlices * kSliceMax);
-                const float *e1 = e0 + kSlices * kSliceMax;
-                auto stage = [&](int c0, int n, bool with_v) {
-                    for (int e = threadIdx.x; e < 2 * n; e += kPThreads)
-                        ebuf[(e >= n) * kCh + (e >= n ? e - n : e)] = __ldcg((e >= n ? e1 + (e - n) : e0 + e) + c0);
-                    if (with_v)
-                        for (int e = threadIdx.x; e < n; e += kPThreads)
-                            vbuf[e] = __ldcg(reinterpret_cast<const uint4 *>(S.v_pages + kv_off(S, pt_sm, l, c0 + e, kvh) + d0));
-                    csync();
-                };
-                const bool one = ctx <= kCh;
-                float lane_acc = 0.0f;             // thread h*8+ln: lane ln of head h
-                for (int c0 = 0; c0 < ctx; c0 += kCh) {
-                    const int n = min(kCh, ctx - c0);
-                    stage(c0, n, one);
-                    if (threadIdx.x < 16) {
-                        const float *eb = ebuf + (threadIdx.x >> 3) * kCh;
-                        const int ln = threadIdx.x & 7;
-                        // t = c0 + k with t = ln mod 8 (c0 is a multiple of 8), t < n8
-                        const int kend = min(n, n8 - c0);
-                        for (int k = ln; k < kend; k += 8) lane_acc = add_rn(lane_acc, eb[k]);
-                    }
-                    if (!one) csync();
-                }
-                if (threadIdx.x < 16) scratch[threadIdx.x] = lane_acc;
-                csync();
-                if (threadIdx.x < 2) {
-                    // the tail (at most 7 positions) from global memory
-                    const float *eh = threadIdx.x ? e1 : e0;
-                    double sum = 0.0;
-                    for (int ln = 0; ln < 8; ++ln) sum = __dadd_rn(sum, (double)scratch[threadIdx.x * 8 + ln]);
-                    for (int t = n8; t < ctx; ++t) sum = __dadd_rn(sum, (double)__ldcg(eh + t));
-                    const bool zero = !isfinite(gm[threadIdx.x]) || !(sum > 0.0) || !isfinite(sum);
-                    scratch[32 + threadIdx.x] = zero ? 0.0f : 1.0f;
-                    scratch[34 + threadIdx.x] = __double2float_rn(__ddiv_rn(1.0, sum));
-                }
-                csync();
-                const int h = threadIdx.x >> 3, j = threadIdx.x & 7;
-                const float inv = threadIdx.x < 16 ? scratch[34 + h] : 0.0f;
-                float a = 0.0f;
-                for (int c0 = 0; c0 < ctx; c0 += kCh) {
-                    const int n = min(kCh, ctx - c0);
-                    if (!one) stage(c0, n, true);
-                    if (threadIdx.x < 16) {
-                        const float *eb = ebuf + h * kCh;
-                        const __half *vb = reinterpret_cast<const __half *>(vbuf) + j;
-                        int k = 0;
-                        for (; k + 8 <= n; k += 8) {
-                            float pv[8], vv[8];
-#pragma unroll
-                            for (int u = 0; u < 8; ++u) {
-                                pv[u] = mul_rn(eb[k + u], inv);
-                                vv[u] = __half2float(vb[(k + u) * 8]);
-                            }
-#pragma unroll
-                            for (int u = 0; u < 8; ++u) a = fma_rn(pv[u], vv[u], a);
-                        }
-                        for (; k < n; ++k) a = fma_rn(mul_rn(eb[k], inv), __half2float(vb[k * 8]), a);
-                    }
-                    if (!one) csync();
-                }
-                if (threadIdx.x < 16) S.att_out[(kvh * 2 + h) * D + d0 + j] = scratch[32 + h] != 0.0f ? a : 0.0f;
-                if (l == 5) DETAIL(255);
-            } else {
             float acc[2][8];
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -898,7 +999,9 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         }
         if (l == 5) DETAIL(247);
         GRID_ARRIVE();
+        if (l == 5) DETAIL_ALL(300);
         stage_norm(W.post_norm + (size_t)l * H, W.post_norm_s + (size_t)l * (H / ng));
+        if (l == 5) DETAIL(248);
         GRID_WAIT_OR_EXIT();
 
         // ---- post-attention rms_norm + quantisation (every CTA), gate/up + SwiGLU
@@ -958,6 +1061,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
         }
         if (l == 5) DETAIL(235);
         GRID_ARRIVE();
+        if (l == 5) DETAIL_ALL(500);
         if (l + 1 < W.layers) stage_norm(W.in_norm + (size_t)(l + 1) * H, W.in_norm_s + (size_t)(l + 1) * (H / ng));
         else stage_norm(W.final_norm, W.final_norm_s);
         GRID_WAIT_OR_EXIT();
