@@ -41,7 +41,7 @@ struct F16Smem {
     static constexpr int kA = kBM * 128;          // 16 KB of weights per stage
     static constexpr int kB = NT * 128;           // activations per stage
     static constexpr int kStage = kA + kB;
-    static constexpr int kSt = NT >= 128 ? 4 : 6;
+    static constexpr int kSt = 4;                 // 128 KB (NT 128) / 96 KB (NT 64: two CTAs per SM)
     static constexpr int kBytes = kSt * kStage + 1024 + 256;
 };
 
@@ -272,7 +272,10 @@ bool gemm_f16_supported(size_t M, size_t N, size_t K) {
 
 cudaError_t launch_gemm_f16_tc(const __half *A, const __half *W, const __half *bias, void *C, int M, int N, int K,
                                int mode, cudaStream_t stream) {
-    const int NT = M >= 512 ? 128 : 64;
+    // 128-row activation tiles only when they alone fill the GPU; otherwise
+    // 64-row tiles (twice the CTAs, two per SM)
+    const long tiles128 = (long)((M + 127) / 128) * ((N + kBM - 1) / kBM);
+    const int NT = (M >= 512 && tiles128 >= 2 * 148) ? 128 : 64;
     CUtensorMap mw, ma;
     if (!map_f16(&mw, W, N, K, kBM) || !map_f16(&ma, A, M, K, NT)) return cudaErrorInvalidValue;
     if (NT == 128) return launch_nt<128>(mw, ma, bias, C, M, N, K, mode, stream);

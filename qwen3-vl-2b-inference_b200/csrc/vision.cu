@@ -160,76 +160,111 @@ __global__ void rotary_kernel(uint16_t *__restrict x, const uint16_t *__restrict
     }
 }
 
-// One warp per (query, head); scores of the query row in shared memory.
-// q, k, v, out fp16 [T, NH, HD] (HD = 64).
-constexpr int kVisWarps = 8;
+// One warp per (query, head), kVQ queries of one head per block, so the
+// head's K and V rows are staged in shared memory once per block (in chunks
+// of kVChunk positions) instead of being read from L2 by every query; the
+// scores of each query row stay in shared memory.  q, k, v, out fp16
+// [T, NH, HD] (HD = 64).
+constexpr int kVQ = 16;
+constexpr int kVChunk = 128;
 constexpr int kVisMaxT = 2048;
-__global__ void __launch_bounds__(kVisWarps * 32)
+constexpr int kKRow = 72;             // halves per staged key row (64 + 8 pad: 4-way banks)
+__global__ void __launch_bounds__(kVQ * 32)
 vision_attention_kernel(const uint16_t *__restrict q, const uint16_t *__restrict k, const uint16_t *__restrict v,
                         uint16_t *__restrict out, int T, int NH, float scale) {
     constexpr int HD = 64;
-    extern __shared__ float sc[];                 // [kVisWarps][T]
+    extern __shared__ __align__(16) unsigned char vsm[];
+    __half *Ks = reinterpret_cast<__half *>(vsm);                       // [kVChunk][kKRow]
+    __half *Vs = Ks + kVChunk * kKRow;                                   // [kVChunk][HD]
+    float *sc = reinterpret_cast<float *>(Vs + kVChunk * HD);            // [kVQ][T]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y;
-    const int i = blockIdx.x * kVisWarps + warp;
-    if (i >= T) return;
+    const int i = blockIdx.x * kVQ + warp;
+    const bool active = i < T;
     float *s = sc + (size_t)warp * T;
     const size_t row = (size_t)NH * HD;
     float qf[HD];
-    const uint4 *qp = reinterpret_cast<const uint4 *>(q + (size_t)i * row + (size_t)h * HD);
-#pragma unroll
-    for (int c = 0; c < HD / 8; ++c) {
-        const uint4 u = qp[c];
-        const __half2 *hh = reinterpret_cast<const __half2 *>(&u);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(hh[j]);
-            qf[8 * c + 2 * j] = f.x;
-            qf[8 * c + 2 * j + 1] = f.y;
-        }
-    }
-    float mx = -INFINITY;
-    for (int t = lane; t < T; t += 32) {
-        const uint4 *kp = reinterpret_cast<const uint4 *>(k + (size_t)t * row + (size_t)h * HD);
-        float a = 0.0f;
+    if (active) {
+        const uint4 *qp = reinterpret_cast<const uint4 *>(q + (size_t)i * row + (size_t)h * HD);
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c) {
-            const uint4 u = __ldg(kp + c);
+            const uint4 u = qp[c];
             const __half2 *hh = reinterpret_cast<const __half2 *>(&u);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float2 f = __half22float2(hh[j]);
-                a = fmaf(qf[8 * c + 2 * j], f.x, a);
-                a = fmaf(qf[8 * c + 2 * j + 1], f.y, a);
+                qf[8 * c + 2 * j] = f.x;
+                qf[8 * c + 2 * j + 1] = f.y;
             }
         }
-        a = __fmul_rn(a, scale);
-        s[t] = a;
-        mx = fmaxf(mx, a);
+    }
+    float mx = -INFINITY;
+    for (int c0 = 0; c0 < T; c0 += kVChunk) {
+        const int n = min(kVChunk, T - c0);
+        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
+            const int r = e >> 3, c = e & 7;
+            reinterpret_cast<uint4 *>(Ks + r * kKRow)[c] =
+                __ldg(reinterpret_cast<const uint4 *>(k + (size_t)(c0 + r) * row + (size_t)h * HD) + c);
+        }
+        __syncthreads();
+        if (active) {
+            for (int t = lane; t < n; t += 32) {
+                const uint4 *kp = reinterpret_cast<const uint4 *>(Ks + t * kKRow);
+                float a = 0.0f;
+#pragma unroll
+                for (int c = 0; c < HD / 8; ++c) {
+                    const uint4 u = kp[c];
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(hh[j]);
+                        a = fmaf(qf[8 * c + 2 * j], f.x, a);
+                        a = fmaf(qf[8 * c + 2 * j + 1], f.y, a);
+                    }
+                }
+                a = __fmul_rn(a, scale);
+                s[c0 + t] = a;
+                mx = fmaxf(mx, a);
+            }
+        }
+        __syncthreads();
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.0f;
-    for (int t = lane; t < T; t += 32) {
-        const float e = exp_ref(__fsub_rn(s[t], mx));
-        s[t] = e;
-        sum += e;
-    }
+    if (active)
+        for (int t = lane; t < T; t += 32) {
+            const float e = exp_ref(__fsub_rn(s[t], mx));
+            s[t] = e;
+            sum += e;
+        }
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     __syncwarp();
     const float inv = __fdiv_rn(1.0f, sum);
     // P.V: lane owns output dims 2*lane, 2*lane+1
     float o0 = 0.0f, o1 = 0.0f;
-    for (int t = 0; t < T; ++t) {
-        const float p = s[t];
-        const __half2 vv = reinterpret_cast<const __half2 *>(v + (size_t)t * row + (size_t)h * HD)[lane];
-        const float2 f = __half22float2(vv);
-        o0 = fmaf(p, f.x, o0);
-        o1 = fmaf(p, f.y, o1);
+    for (int c0 = 0; c0 < T; c0 += kVChunk) {
+        const int n = min(kVChunk, T - c0);
+        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
+            const int r = e >> 3, c = e & 7;
+            reinterpret_cast<uint4 *>(Vs + r * HD)[c] =
+                __ldg(reinterpret_cast<const uint4 *>(v + (size_t)(c0 + r) * row + (size_t)h * HD) + c);
+        }
+        __syncthreads();
+        if (active)
+            for (int t = 0; t < n; ++t) {
+                const float p = s[c0 + t];
+                const float2 f = __half22float2(reinterpret_cast<const __half2 *>(Vs + t * HD)[lane]);
+                o0 = fmaf(p, f.x, o0);
+                o1 = fmaf(p, f.y, o1);
+            }
+        __syncthreads();
     }
-    __half2 r = __floats2half2_rn(__fmul_rn(o0, inv), __fmul_rn(o1, inv));
-    reinterpret_cast<__half2 *>(out + (size_t)i * row + (size_t)h * HD)[lane] = r;
+    if (active) {
+        __half2 r = __floats2half2_rn(__fmul_rn(o0, inv), __fmul_rn(o1, inv));
+        reinterpret_cast<__half2 *>(out + (size_t)i * row + (size_t)h * HD)[lane] = r;
+    }
 }
 
 cudaError_t launch_patch_embed(const float *img, const uint16_t *w, const uint16_t *b, float *out, int T, int N, int K,
@@ -264,12 +299,12 @@ cudaError_t launch_vision_rotary(uint16_t *x, const uint16_t *cs, const uint16_t
 
 cudaError_t launch_vision_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out, int T,
                                     int NH, float scale, cudaStream_t st) {
-    const size_t smem = (size_t)kVisWarps * T * sizeof(float);
+    const size_t smem = (size_t)kVChunk * kKRow * 2 + (size_t)kVChunk * 64 * 2 + (size_t)kVQ * T * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(vision_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((T + kVisWarps - 1) / kVisWarps, NH);
-    vision_attention_kernel<<<grid, kVisWarps * 32, smem, st>>>(q, k, v, out, T, NH, scale);
+    dim3 grid((T + kVQ - 1) / kVQ, NH);
+    vision_attention_kernel<<<grid, kVQ * 32, smem, st>>>(q, k, v, out, T, NH, scale);
     return cudaGetLastError();
 }
 
