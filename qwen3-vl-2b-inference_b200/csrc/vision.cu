@@ -160,9 +160,15 @@ __global__ void rotary_kernel(uint16_t *__restrict x, const uint16_t *__restrict
     }
 }
 
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
 // One warp per (query, head), kVQ queries of one head per block, so the
-// head's K and V rows are staged in shared memory once per block (in chunks
-// of kVChunk positions) instead of being read from L2 by every query; the
+// head's K and V rows are staged in shared memory once per block -- chunks of
+// kVChunk positions, double-buffered with cp.async so the next chunk loads
+// while this one is used -- instead of being read from L2 by every query; the
 // scores of each query row stay in shared memory.  q, k, v, out fp16
 // [T, NH, HD] (HD = 64).
 constexpr int kVQ = 16;
@@ -174,15 +180,35 @@ vision_attention_kernel(const uint16_t *__restrict q, const uint16_t *__restrict
                         uint16_t *__restrict out, int T, int NH, float scale) {
     constexpr int HD = 64;
     extern __shared__ __align__(16) unsigned char vsm[];
-    __half *Ks = reinterpret_cast<__half *>(vsm);                       // [kVChunk][kKRow]
-    __half *Vs = Ks + kVChunk * kKRow;                                   // [kVChunk][HD]
-    float *sc = reinterpret_cast<float *>(Vs + kVChunk * HD);            // [kVQ][T]
+    __half *Ks = reinterpret_cast<__half *>(vsm);                       // [2][kVChunk][kKRow]
+    __half *Vs = Ks + 2 * kVChunk * kKRow;                               // [2][kVChunk][HD]
+    float *sc = reinterpret_cast<float *>(Vs + 2 * kVChunk * HD);        // [kVQ][T]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y;
     const int i = blockIdx.x * kVQ + warp;
     const bool active = i < T;
     float *s = sc + (size_t)warp * T;
     const size_t row = (size_t)NH * HD;
+    const int nch = (T + kVChunk - 1) / kVChunk;
+    auto issue_k = [&](int c) {
+        const int c0 = c * kVChunk, n = min(kVChunk, T - c0);
+        __half *dst = Ks + (c & 1) * kVChunk * kKRow;
+        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
+            const int r = e >> 3, cc = e & 7;
+            cp16(dst + r * kKRow + cc * 8, k + (size_t)(c0 + r) * row + (size_t)h * HD + cc * 8);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto issue_v = [&](int c) {
+        const int c0 = c * kVChunk, n = min(kVChunk, T - c0);
+        __half *dst = Vs + (c & 1) * kVChunk * HD;
+        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
+            const int r = e >> 3, cc = e & 7;
+            cp16(dst + r * HD + cc * 8, v + (size_t)(c0 + r) * row + (size_t)h * HD + cc * 8);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue_k(0);
     float qf[HD];
     if (active) {
         const uint4 *qp = reinterpret_cast<const uint4 *>(q + (size_t)i * row + (size_t)h * HD);
@@ -199,27 +225,30 @@ vision_attention_kernel(const uint16_t *__restrict q, const uint16_t *__restrict
         }
     }
     float mx = -INFINITY;
-    for (int c0 = 0; c0 < T; c0 += kVChunk) {
-        const int n = min(kVChunk, T - c0);
-        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
-            const int r = e >> 3, c = e & 7;
-            reinterpret_cast<uint4 *>(Ks + r * kKRow)[c] =
-                __ldg(reinterpret_cast<const uint4 *>(k + (size_t)(c0 + r) * row + (size_t)h * HD) + c);
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+            issue_k(c + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            issue_v(0);                      // V's first chunk loads during the last scores
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
         }
         __syncthreads();
+        const int c0 = c * kVChunk, n = min(kVChunk, T - c0);
+        const __half *kb = Ks + (c & 1) * kVChunk * kKRow;
         if (active) {
             for (int t = lane; t < n; t += 32) {
-                const uint4 *kp = reinterpret_cast<const uint4 *>(Ks + t * kKRow);
+                const uint4 *kp = reinterpret_cast<const uint4 *>(kb + t * kKRow);
                 float a = 0.0f;
 #pragma unroll
-                for (int c = 0; c < HD / 8; ++c) {
-                    const uint4 u = kp[c];
+                for (int cc = 0; cc < HD / 8; ++cc) {
+                    const uint4 u = kp[cc];
                     const __half2 *hh = reinterpret_cast<const __half2 *>(&u);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const float2 f = __half22float2(hh[j]);
-                        a = fmaf(qf[8 * c + 2 * j], f.x, a);
-                        a = fmaf(qf[8 * c + 2 * j + 1], f.y, a);
+                        a = fmaf(qf[8 * cc + 2 * j], f.x, a);
+                        a = fmaf(qf[8 * cc + 2 * j + 1], f.y, a);
                     }
                 }
                 a = __fmul_rn(a, scale);
@@ -244,18 +273,20 @@ vision_attention_kernel(const uint16_t *__restrict q, const uint16_t *__restrict
     const float inv = __fdiv_rn(1.0f, sum);
     // P.V: lane owns output dims 2*lane, 2*lane+1
     float o0 = 0.0f, o1 = 0.0f;
-    for (int c0 = 0; c0 < T; c0 += kVChunk) {
-        const int n = min(kVChunk, T - c0);
-        for (int e = threadIdx.x; e < n * (HD / 8); e += blockDim.x) {
-            const int r = e >> 3, c = e & 7;
-            reinterpret_cast<uint4 *>(Vs + r * HD)[c] =
-                __ldg(reinterpret_cast<const uint4 *>(v + (size_t)(c0 + r) * row + (size_t)h * HD) + c);
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+            issue_v(c + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
+        const int c0 = c * kVChunk, n = min(kVChunk, T - c0);
+        const __half *vb = Vs + (c & 1) * kVChunk * HD;
         if (active)
             for (int t = 0; t < n; ++t) {
                 const float p = s[c0 + t];
-                const float2 f = __half22float2(reinterpret_cast<const __half2 *>(Vs + t * HD)[lane]);
+                const float2 f = __half22float2(reinterpret_cast<const __half2 *>(vb + t * HD)[lane]);
                 o0 = fmaf(p, f.x, o0);
                 o1 = fmaf(p, f.y, o1);
             }
@@ -299,7 +330,7 @@ cudaError_t launch_vision_rotary(uint16_t *x, const uint16_t *cs, const uint16_t
 
 cudaError_t launch_vision_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out, int T,
                                     int NH, float scale, cudaStream_t st) {
-    const size_t smem = (size_t)kVChunk * kKRow * 2 + (size_t)kVChunk * 64 * 2 + (size_t)kVQ * T * sizeof(float);
+    const size_t smem = 2 * ((size_t)kVChunk * kKRow * 2 + (size_t)kVChunk * 64 * 2) + (size_t)kVQ * T * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(vision_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
