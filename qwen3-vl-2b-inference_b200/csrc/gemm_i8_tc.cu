@@ -337,7 +337,14 @@ cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M,
 cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
                                      const float *ws, float *C, int M, int N, int K, int acc,
                                      cudaStream_t stream) {
-    const int NT = M >= 256 ? 128 : (M >= 64 ? 64 : 32);
+    // the widest activation tile that still gives ~one CTA per SM: narrower
+    // tiles (and, at 32 rows, split-K) for small-N products such as the k / v
+    // projections of a prompt
+    const long nt128 = (long)((N + kBM - 1) / kBM) * ((M + 127) / 128);
+    const long nt64 = (long)((N + kBM - 1) / kBM) * ((M + 63) / 64);
+    const int NT = M >= 512 ? 128
+                   : (M >= 256 && nt128 >= 148) ? 128
+                   : (M >= 64 && nt64 >= 148) ? 64 : 32;
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
