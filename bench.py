@@ -326,7 +326,8 @@ def run_gemv(dev, steps=640, warmup=5):
         raise SystemExit("bench: config-0 GEMV output differs from the oracle")
     del wc
     return {"workload": WORKLOAD, "step_gbs": round(out["step"], 1), "kernel_gbs": round(out["kernel"], 1),
-            "launches_per_step": 2, "steps": steps}
+            "launches_per_step": 1, "step": "linear(): the activation quantisation inside the ring GEMV",
+            "steps": steps}
 
 
 def ctypes_byref(x):

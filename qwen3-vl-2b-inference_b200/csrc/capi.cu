@@ -214,6 +214,15 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
     int16_t *q = static_cast<int16_t *>(workspace);
     float *qs = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * K * 2));
     cudaStream_t st = (cudaStream_t)stream;
+    // M = 1 per-row products large enough for the ring GEMV: the activation
+    // quantisation happens inside it (one launch instead of two)
+    if (M == 1 && g == K && lane8_for(semantics, M, N, K) && N * K >= kRingMinBytes && ring_enabled()) {
+        qvl::RingGemvArgs r{nullptr, nullptr, B, B_scales, C, (int)N, (int)K, acc, A};
+        if (qvl::gemv_ring_supported(r)) {
+            QVL_CUDA_TRY(qvl::launch_gemv_ring(r, st));
+            return QVL_OK;
+        }
+    }
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
     void *planes = nullptr;
     if (M >= 16 && g == K && K % 128 == 0 &&

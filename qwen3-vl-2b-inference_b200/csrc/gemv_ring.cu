@@ -10,6 +10,7 @@
 // warp w takes row w of every stage; a K = 6144 row spans three stages, its
 // int32 lane sums carried across them (exact).  Every wait is bounded.
 #include "ring_common.cuh"
+#include "qact.cuh"
 #include "gemv_ring.cuh"
 
 namespace qvl {
@@ -35,6 +36,7 @@ __global__ void __launch_bounds__(kBlock, 1) gemv_ring_kernel(RingGemvArgs a) {
     __shared__ __align__(8) uint64_t full_mb[kStagesR], empty_mb[kStagesR];
     __shared__ __align__(16) float scl[kStagesR][kRows];
     __shared__ int stop_flag, prod_done, issued_sh;
+    __shared__ float a_s_sh, inv_sh;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t ring = tc::smem_u32(sm), full = tc::smem_u32(full_mb), empty = tc::smem_u32(empty_mb);
     const uint32_t ring_s = tc::smem_u32(&scl[0][0]);
@@ -85,9 +87,33 @@ __global__ void __launch_bounds__(kBlock, 1) gemv_ring_kernel(RingGemvArgs a) {
 
     // compute warps: the activations are the previous kernel's output
     pdl_wait();
-    for (int i = threadIdx.x; i < a.K / 8; i += kThreads)
-        reinterpret_cast<int4 *>(q16)[i] = reinterpret_cast<const int4 *>(a.q)[i];
-    const float a_s = a.qs[0];
+    float a_s;
+    if (a.x) {
+        // the activation quantisation of the reference's linear() (one group
+        // of K), done by every CTA while its weight stages stream in:
+        // fp32 row into shared memory, warp 0 forms the scale (the 16-lane
+        // fused chain of group_sumsq_ref, both half-warps), all threads quantise
+        float *xs = reinterpret_cast<float *>(q16 + a.K);
+        for (int i = threadIdx.x; i < a.K / 4; i += kThreads)
+            reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(a.x)[i];
+        csync();
+        if (threadIdx.x < 32) {
+            const float ss = group_sumsq_ref(xs, a.K, threadIdx.x & 15);
+            const float s = mul_rn(__fsqrt_rn(fma_rn(ss, __fdiv_rn(1.0f, (float)a.K), 1e-6f)), inv127());
+            if (threadIdx.x == 0) {
+                a_s_sh = s;
+                inv_sh = __fdiv_rn(1.0f, s);
+            }
+        }
+        csync();
+        const float inv = inv_sh;
+        for (int j = threadIdx.x; j < a.K; j += kThreads) q16[j] = quant_one(xs[j], inv);
+        a_s = a_s_sh;
+    } else {
+        for (int i = threadIdx.x; i < a.K / 8; i += kThreads)
+            reinterpret_cast<int4 *>(q16)[i] = reinterpret_cast<const int4 *>(a.q)[i];
+        a_s = a.qs[0];
+    }
     csync();
     const int4 *q_s = reinterpret_cast<const int4 *>(q16);
     Act act;
@@ -127,7 +153,9 @@ __global__ void __launch_bounds__(kBlock, 1) gemv_ring_kernel(RingGemvArgs a) {
     }
 }
 
-size_t ring_smem_bytes(int K) { return (size_t)kStagesR * kStageBytes + (size_t)K * sizeof(int16_t); }
+size_t ring_smem_bytes(int K, bool fused) {
+    return (size_t)kStagesR * kStageBytes + (size_t)K * sizeof(int16_t) + (fused ? (size_t)K * sizeof(float) : 0);
+}
 
 int ring_grid(int N) {
     static int sms[64] = {};
@@ -142,22 +170,24 @@ int ring_grid(int N) {
 }  // namespace
 
 bool gemv_ring_supported(const RingGemvArgs &a) {
+    if (a.x ? (a.K > kRingFusedMaxK || ((uintptr_t)a.x & 15)) : ((uintptr_t)a.q & 15) != 0) return false;
     return a.N >= kRows && a.N % kRows == 0 && a.K >= kSegBytes && a.K % kSegBytes == 0 && a.K <= kMaxK &&
-           ((uintptr_t)a.W & 15) == 0 && ((uintptr_t)a.Ws & 15) == 0 && ((uintptr_t)a.q & 15) == 0;
+           ((uintptr_t)a.W & 15) == 0 && ((uintptr_t)a.Ws & 15) == 0;
 }
 
 cudaError_t launch_gemv_ring(const RingGemvArgs &a, cudaStream_t st) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)ring_smem_bytes(kMaxK));
+        const size_t mx = ring_smem_bytes(kMaxK, false) > ring_smem_bytes(kRingFusedMaxK, true)
+                              ? ring_smem_bytes(kMaxK, false) : ring_smem_bytes(kRingFusedMaxK, true);
+        cudaError_t e = cudaFuncSetAttribute(gemv_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ring_grid(a.N));
     cfg.blockDim = dim3(kBlock);
-    cfg.dynamicSmemBytes = ring_smem_bytes(a.K);
+    cfg.dynamicSmemBytes = ring_smem_bytes(a.K, a.x != nullptr);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

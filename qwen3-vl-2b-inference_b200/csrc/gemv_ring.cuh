@@ -15,11 +15,15 @@ struct RingGemvArgs {
     const float *Ws;      // [N]
     float *y;             // [N]
     int N, K, acc;
+    // fp32 activations [K] to quantise inside the kernel (the reference's
+    // per-row activation quantisation, group K) instead of q / qs; K <= 4096
+    const float *x = nullptr;
 };
 
 // Shapes the ring GEMV takes: N a multiple of 16, K a multiple of 2048 up to
 // 6144, 16-byte aligned weights and scales.
 bool gemv_ring_supported(const RingGemvArgs &a);
+constexpr int kRingFusedMaxK = 4096;
 cudaError_t launch_gemv_ring(const RingGemvArgs &a, cudaStream_t st);
 
 }  // namespace qvl
