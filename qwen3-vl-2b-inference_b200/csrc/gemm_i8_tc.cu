@@ -39,6 +39,10 @@ constexpr int kUmmaK = 32;        // K per kind::i8 MMA
 // qvl_tc_timeout_word().
 __device__ int g_gemm_tc_timeout = 0;
 
+__device__ __forceinline__ void mbar_arrive_cta(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 template <int NT>
 struct TcSmem {
     static constexpr int kA = kBM * kBK;          // 16 KB
@@ -227,6 +231,176 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     if (warp == 1) tc::tmem_dealloc(tmem, kCols);
 }
 
+// Persistent form for large products (M >= 512, many tiles): one CTA per SM
+// walks the tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (activation
+// tile fastest, so the CTAs working at the same time share weight tiles in
+// L2).  Warp 0 issues the TMA loads of a 4-stage ring across tile boundaries,
+// warp 1 the MMAs, and warps 2-5 drain the accumulators; the accumulators are
+// double-buffered in tensor memory (2 x hi/lo x NT columns = all 512 columns
+// at NT = 128), so the epilogue of tile i overlaps the main loop of tile i+1.
+// Same arithmetic as gemm_i8_tc_kernel (exact int32 sums, the reference's fp32
+// epilogue); every wait is bounded.
+constexpr int kPersistThreads = 192;
+template <int NT>
+struct TcPersistSmem {
+    static constexpr int kA = kBM * kBK;
+    static constexpr int kB = NT * kBK;
+    static constexpr int kStage = kA + 2 * kB;
+    static constexpr int kSt = 4;
+    static constexpr int kBytes = kSt * kStage + 1024 + 256;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+gemm_i8_tc_persistent(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
+                      const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
+                      const float *__restrict w_scale, float *__restrict C, int M, int N, int K, int acc) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    using L = TcPersistSmem<NT>;
+    constexpr int kS = L::kSt;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kS * L::kStage);
+    const uint32_t full0 = tc::smem_u32(bars);                 // [kS]
+    const uint32_t empty0 = tc::smem_u32(bars + kS);           // [kS]
+    const uint32_t tfull0 = tc::smem_u32(bars + 2 * kS);       // [2] accumulator b complete
+    const uint32_t tempty0 = tc::smem_u32(bars + 2 * kS + 2);  // [2] accumulator b drained
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kS + 4);
+    __shared__ int timed_out_at_entry;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (M + NT - 1) / NT, ntl = (N + kBM - 1) / kBM;
+    const int tiles = mt * ntl;
+    const int nk = K / kBK;
+    constexpr uint32_t kCols = 4 * NT;           // 2 buffers x (hi, lo)
+
+    if (threadIdx.x == 0) {
+        timed_out_at_entry = *reinterpret_cast<volatile int *>(&g_gemm_tc_timeout) != 0;
+        for (int i = 0; i < kS; ++i) {
+            tc::mbar_init(full0 + 8 * i, 1);
+            tc::mbar_init(empty0 + 8 * i, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(tfull0 + 8 * b, 1);
+            tc::mbar_init(tempty0 + 8 * b, 4);    // one elected lane per epilogue warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        tc::prefetch_tmap(&tm_w);
+        tc::prefetch_tmap(&tm_hi);
+        tc::prefetch_tmap(&tm_lo);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
+    bool ok = !timed_out_at_entry;
+    int issued = 0;
+
+    if (warp == 0) {
+        if (lane == 0 && ok) {
+            int kk = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % mt) * NT, n0 = (t / mt) * kBM;
+                for (int kb = 0; kb < nk && ok; ++kb, ++kk) {
+                    const int s = kk % kS;
+                    if (kk >= kS) ok = tc::mbar_wait(empty0 + 8 * s, ((kk / kS) - 1) & 1, &g_gemm_tc_timeout);
+                    if (!ok) break;
+                    unsigned char *st = smem + s * L::kStage;
+                    tc::mbar_expect_tx(full0 + 8 * s, L::kStage);
+                    tc::tma_load_2d(tc::smem_u32(st), &tm_w, kb * kBK, n0, full0 + 8 * s);
+                    if (kk == 0) pdl_wait();   // activations come from the previous kernel
+                    tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, kb * kBK, m0, full0 + 8 * s);
+                    tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, kb * kBK, m0, full0 + 8 * s);
+                    issued = kk + 1;
+                }
+            }
+            if (!ok) {
+                // wait (bounded) for the copies already issued, so that none
+                // lands in shared memory after the CTA has left
+                for (int k2 = issued - 1; k2 >= 0 && k2 >= issued - kS; --k2)
+                    tc::mbar_wait(full0 + 8 * (k2 % kS), (k2 / kS) & 1, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && ok) {
+            constexpr uint32_t id_hi = tc::idesc_i8(kBM, NT, true);
+            constexpr uint32_t id_lo = tc::idesc_i8(kBM, NT, false);
+            int kk = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+                const int b = i & 1, u = i >> 1;
+                if (u >= 1) ok = tc::mbar_wait(tempty0 + 8 * b, (u - 1) & 1, &g_gemm_tc_timeout);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint32_t d_hi = tmem + (uint32_t)(b * 2 * NT), d_lo = d_hi + NT;
+                for (int kb = 0; kb < nk && ok; ++kb, ++kk) {
+                    const int s = kk % kS;
+                    ok = tc::mbar_wait(full0 + 8 * s, (kk / kS) & 1, &g_gemm_tc_timeout);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint32_t a_base = tc::smem_u32(smem + s * L::kStage);
+                    const uint32_t h_base = a_base + L::kA;
+                    const uint32_t l_base = h_base + L::kB;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k) {
+                        const uint64_t ad = tc::sdesc_k_sw128(a_base + k * kUmmaK);
+                        const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+                        tc::mma_i8(d_hi, ad, tc::sdesc_k_sw128(h_base + k * kUmmaK), id_hi, accum);
+                        tc::mma_i8(d_lo, ad, tc::sdesc_k_sw128(l_base + k * kUmmaK), id_lo, accum);
+                    }
+                    tc::tc_commit(empty0 + 8 * s);
+                }
+                if (ok) tc::tc_commit(tfull0 + 8 * b);
+            }
+        }
+    } else {
+        // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31 = weight rows
+        pdl_wait();
+        const int q4 = warp & 3;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+            const int m0 = (t % mt) * NT, n0 = (t / mt) * kBM;
+            const int b = i & 1, u = i >> 1;
+            ok = tc::mbar_wait(tfull0 + 8 * b, u & 1, &g_gemm_tc_timeout);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc::tc_fence_after();
+            const uint32_t d_hi = tmem + (uint32_t)(b * 2 * NT), d_lo = d_hi + NT;
+            const int n = n0 + q4 * 32 + lane;
+            const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < NT; c0 += 16) {
+                uint32_t hi[16], lo[16];
+                tc::tmem_ld16(d_hi + lane_off + c0, hi);
+                tc::tmem_ld16(d_lo + lane_off + c0, lo);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m < M && n < N) {
+                        const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
+                        const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
+                        const float v = fma_rn(p, ws, 0.0f);
+                        float *cp = C + (size_t)m * N + n;
+                        *cp = acc ? add_rn(*cp, v) : v;
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cta(tempty0 + 8 * b);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, kCols);
+}
+
 // q int16 [M, K] -> hi int8 [M, K] (q >> 8), lo uint8 [M, K] (q & 255).
 __global__ void split_hi_lo_kernel(const int16_t *__restrict q, int8_t *__restrict hi, uint8_t *__restrict lo,
                                    long n) {
@@ -305,12 +479,45 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
     return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
 }
 
+template <int NT>
+cudaError_t launch_persistent(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
+                              const float *ws, float *C, int M, int N, int K, int acc, cudaStream_t st) {
+    auto kern = gemm_i8_tc_persistent<NT>;
+    const int smem = TcPersistSmem<NT>::kBytes;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long tiles = (long)((M + NT - 1) / NT) * ((N + kBM - 1) / kBM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles < sms ? tiles : sms));
+    cfg.blockDim = dim3(kPersistThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
+}
+
 }  // namespace
 
 int *gemm_tc_timeout_word() {
     void *p = nullptr;
     if (cudaGetSymbolAddress(&p, g_gemm_tc_timeout) != cudaSuccess) return nullptr;
     return static_cast<int *>(p);
+}
+
+// QVL_GEMM_PERSIST=0 in the environment keeps the one-tile-per-CTA kernel.
+static bool persist_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("QVL_GEMM_PERSIST");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
 }
 
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
@@ -348,7 +555,12 @@ cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const 
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
-    if (NT == 128) return launch_nt<128, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 128) {
+        // many tiles: the persistent kernel (double-buffered accumulators)
+        if (persist_enabled() && (long)((M + 127) / 128) * ((N + kBM - 1) / kBM) >= 2 * 148)
+            return launch_persistent<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+        return launch_nt<128, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    }
     if (NT == 64) return launch_nt<64, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
     // small M (decode batches): split K over a cluster until ~2 CTAs per SM
     const long tiles = (long)((N + kBM - 1) / kBM) * ((M + 31) / 32);

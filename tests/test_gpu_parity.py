@@ -328,13 +328,32 @@ def test_argmax_tie_and_nan(qvl, cuda):
 # ------------------------------------------------------------ tensor-core GEMM
 @pytest.mark.parametrize("M,N,K", [(16, 128, 128), (32, 2048, 2048), (32, 1024, 2048), (32, 2048, 6144),
                                    (17, 256, 1024), (48, 6144, 2048), (512, 2048, 2048), (512, 1024, 2048), (512, 6144, 2048),
-                                   (512, 2048, 6144), (130, 2048, 2048), (2048, 256, 2048), (77, 300, 1024)])
+                                   (512, 2048, 6144), (130, 2048, 2048), (2048, 256, 2048), (77, 300, 1024),
+                                   (454, 1024, 2048), (454, 6144, 2048),
+                                   (1024, 6144, 2048), (600, 8192, 1024)])
 def test_linear_prefill_tensor_core_bit_exact(qvl, cuda, M, N, K):
     """M >= 16 with per-row scales runs the tcgen05 kind::i8 GEMM (hi/lo split
-    of the int16 activations); TILED order, bit-exact with the oracle."""
+    of the int16 activations); TILED order, bit-exact with the oracle.  The
+    last two shapes have >= 2 waves of 128 x 128 tiles and take the
+    persistent kernel (double-buffered accumulators; 600 rows: a ragged
+    activation tile)."""
     x, w, ws = make_linear_inputs(7 * M + N, M, N, K, K)
     y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=False)
-    np.testing.assert_array_equal(y.cpu().numpy(), oracle.linear_i8(x, w, ws, K, oracle.TILED))
+    np.testing.assert_array_equal(y.cpu().numpy(), oracle.linear_i8(x, w, ws, K, oracle.TILED, threads=16))
+
+
+def test_linear_persistent_tensor_core_accumulate(qvl, cuda):
+    """C += product on the persistent tensor-core path (the reference's
+    add_vector after linear()), bit-exact."""
+    M, N, K = 600, 8192, 1024
+    x, w, ws = make_linear_inputs(99, M, N, K, K)
+    q, qs = qvl.quantize_rows(dev(x, cuda), K)
+    c0 = np.random.default_rng(5).standard_normal((M, N), dtype=np.float32)
+    c = dev(c0.copy(), cuda)
+    qvl.linear_batched(q, qs, [(dev(w, cuda), dev(ws, cuda))], [c], qvl.Workspace(cuda),
+                       semantics=qvl.SEM_TILED | qvl.SEM_ACCUMULATE)
+    want = (c0 + oracle.linear_i8(x, w, ws, K, oracle.TILED, threads=16)).astype(np.float32)
+    np.testing.assert_array_equal(c.cpu().numpy(), want)
 
 
 @pytest.mark.parametrize("M", [64, 512])
