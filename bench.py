@@ -616,7 +616,7 @@ def run_prefill_gemm(args):
         roofline_gemm = {"bound": "tensor", "achieved": round(tops / ws, 2), "peak": i8peak, "unit": "TOPS",
                          "frac": round(tops / ws / i8peak, 4) if i8peak else None,
                          "peak_kind": "measured (torch._int_mm int8, 8192^3, this GPU)", "traffic": None,
-                         "kernel": "gemm_i8_tc_kernel (tcgen05 kind::i8, hi/lo planes: 2 MMAs per algorithmic one)"}
+                         "kernel": "gemm_i8_tc (tcgen05 kind::i8; persistent for the LM head, split-K clusters for the rest; hi/lo planes: 2 MMAs per algorithmic one)"}
         import oracle
         X, W, S, Y = mats[0]
         ref = oracle.linear_i8(X[:2].cpu().numpy(), W.cpu().numpy(), S.cpu().numpy(), 2048, oracle.TILED)
@@ -628,7 +628,7 @@ def run_prefill_gemm(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32", "data": "synthetic",
             "config": {"workload": f"config1_gemm_M{M}", "shapes_NK": PREFILL_SHAPES,
                        "ops_per_step": ops, "note": "ops = 2*M*N*K (the hi/lo split doubles the MMA work)"},
-            "roofline": roofline_gemm, "clocks": clk.summary(), "gpu_launches": 3 * len(PREFILL_SHAPES) * args.steps,
+            "roofline": roofline_gemm, "clocks": clk.summary(), "gpu_launches": 2 * len(PREFILL_SHAPES) * args.steps,
         }))
     if ws > 1:
         dist.destroy_process_group()

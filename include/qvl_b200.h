@@ -81,7 +81,8 @@ const char *qvl_version(void);
  *      cpu_f32a_i8f32sb_f32c_avx2.cpp:135-177, :348-390, :488-530) ---------
  * x fp32 [M, K] -> q int16 [M, K], q_scales fp32 [M, K / group_size]:
  * s = sqrtf(sum(x^2) / g + 1e-6) / 127 per group, q = sat16(rne(x / s)).
- * Requires K % group_size == 0 and group_size % 16 == 0. */
+ * Requires K % group_size == 0, group_size % 16 == 0, x 16-byte and q
+ * 8-byte aligned. */
 int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales,
                       size_t M, size_t K, size_t group_size, void *stream);
 
@@ -170,7 +171,8 @@ int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);
 
 /* swiglu followed by the down projection's activation quantisation, without
  * materialising the fp32 SwiGLU output: q/q_scales = quantize_rows(
- * swiglu(gate, up)) for M rows of I values (gate/up are not modified). */
+ * swiglu(gate, up)) for M rows of I values (gate/up are not modified;
+ * gate/up 16-byte and q 8-byte aligned). */
 int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, float *q_scales,
                              size_t M, size_t I, size_t group_size, void *stream);
 

@@ -53,19 +53,12 @@ bool lane8_for(int semantics, size_t M, size_t N, size_t K) {
     return M == 1 && N >= 1024 && K >= 1024;   // cpu_f32a_i8f32sb_f32c_avx2.cpp:464
 }
 
-// y[M,N] from pre-quantised activations: CUDA-core GEMV for small M (and for
-// the LANE8 summation order at any M), tensor cores for TILED at M >= 16.
-// tc_planes: workspace for the tensor-core path's hi/lo activation planes
-// (gemm_tc_planes_bytes); nullptr keeps the product on the CUDA-core GEMV.
+// y[M,N] from pre-quantised activations on the CUDA cores: the ring GEMV
+// for large single-row products, else the tiled GEMV in row tiles.  (The
+// tensor-core products are launched by the callers on hi/lo planes that their
+// quantisation kernels write.)
 int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const float *Bs, float *C,
-                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st, int acc = 0,
-                   void *tc_planes = nullptr) {
-    if (tc_planes && !lane8 && !acc && qvl::gemm_tc_supported(M, N, K, g)) {
-        int8_t *hi = static_cast<int8_t *>(tc_planes);
-        uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, K) / 2;
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc(q, qs, hi, lo, B, Bs, C, (int)M, (int)N, (int)K, st));
-        return QVL_OK;
-    }
+                   size_t M, size_t N, size_t K, size_t g, bool lane8, cudaStream_t st, int acc = 0) {
     if (M == 1 && lane8 && g == K && N * K >= kRingMinBytes && ring_enabled()) {
         qvl::RingGemvArgs r{q, qs, B, Bs, C, (int)N, (int)K, acc};
         if (qvl::gemv_ring_supported(r)) {
@@ -170,7 +163,7 @@ int qvl_internal_set_tc_timeout(void *stream) {
 int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, size_t K,
                       size_t group_size, void *stream) {
     if (!x || !q || !q_scales) return QVL_ERR_INVALID;
-    if (!aligned(x, 16)) return QVL_ERR_INVALID;
+    if (!aligned(x, 16) || !aligned(q, 8)) return QVL_ERR_INVALID;
     if (M == 0 || K == 0 || group_size == 0 || K % group_size || group_size % 16) return QVL_ERR_INVALID;
     QVL_CUDA_TRY(qvl::launch_quantize_rows(x, q, q_scales, (int)M, (int)K, (int)group_size,
                                            (cudaStream_t)stream));
@@ -223,12 +216,18 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
             return QVL_OK;
         }
     }
+    const bool lane8 = lane8_for(semantics, M, N, K);
+    // tensor-core product: the quantisation writes its hi/lo planes directly
+    if (!lane8 && !acc && workspace_bytes >= need + qvl::gemm_tc_planes_bytes(M, K) &&
+        qvl::gemm_tc_supported(M, N, K, g)) {
+        int8_t *hi = reinterpret_cast<int8_t *>(static_cast<char *>(workspace) + need);
+        uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, K) / 2;
+        QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st, hi, lo));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo, qs, B, B_scales, C, (int)M, (int)N, (int)K, 0, st));
+        return QVL_OK;
+    }
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
-    void *planes = nullptr;
-    if (M >= 16 && g == K && K % 128 == 0 &&
-        workspace_bytes >= need + qvl::gemm_tc_planes_bytes(M, K))
-        planes = static_cast<char *>(workspace) + need;
-    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8_for(semantics, M, N, K), st, acc, planes);
+    return run_q16_linear(q, qs, B, B_scales, C, M, N, K, g, lane8, st, acc);
 }
 
 int qvl_linear_q16_i8_multi(const int16_t *q, const float *q_scales, size_t n_mats,
@@ -449,23 +448,39 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
     int16_t *qh = reinterpret_cast<int16_t *>(w);
     float *qhs = reinterpret_cast<float *>(w + align256(M * I * 2));
     w += qbuf_bytes(M, I, g_h);
-    void *planes = w;        // hi/lo activation planes of the tensor-core path (M >= 16, TILED)
+    // hi/lo activation planes of the tensor-core path (M >= 16, TILED), written
+    // by the quantisation kernels themselves
+    int8_t *hi = reinterpret_cast<int8_t *>(w);
     cudaStream_t st = (cudaStream_t)stream;
-    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)g_in, st));
-    const bool l_gu = lane8_for(semantics, M, I, H);
-    rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, g_in, l_gu, st, 0, planes);
-    if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, g_in, l_gu, st, 0, planes);
-    if (rc) return rc;
-    if (g_h >= 4096) {
+    const bool l_gu = lane8_for(semantics, M, I, H), l_d = lane8_for(semantics, M, H, I);
+    const bool tc_gu = !l_gu && qvl::gemm_tc_supported(M, I, H, g_in);
+    const bool tc_d = !l_d && qvl::gemm_tc_supported(M, H, I, g_h);
+    uint8_t *lo_gu = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, H) / 2;
+    uint8_t *lo_d = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, I) / 2;
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)g_in, st, tc_gu ? hi : nullptr,
+                                           tc_gu ? lo_gu : nullptr));
+    if (tc_gu) {
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wg, sg, gate, (int)M, (int)I, (int)H, 0, st));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wu, su, up, (int)M, (int)I, (int)H, 0, st));
+    } else {
+        rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, g_in, l_gu, st);
+        if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, g_in, l_gu, st);
+        if (rc) return rc;
+    }
+    if (g_h >= 4096 || tc_d) {
         // whole-row groups: the SwiGLUs (double-precision exp) spread over the
         // GPU in place in the gate scratch, then the row quantisation
         QVL_CUDA_TRY(qvl::launch_swiglu(gate, up, (long)(M * I), st));
-        QVL_CUDA_TRY(qvl::launch_quantize_rows(gate, qh, qhs, (int)M, (int)I, (int)g_h, st));
+        QVL_CUDA_TRY(qvl::launch_quantize_rows(gate, qh, qhs, (int)M, (int)I, (int)g_h, st, tc_d ? hi : nullptr,
+                                               tc_d ? lo_d : nullptr));
     } else {
         QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)g_h, st));
     }
-    return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, g_h,
-                          lane8_for(semantics, M, H, I), st, 0, planes);
+    if (tc_d) {
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_d, qhs, Wd, sd, out, (int)M, (int)H, (int)I, 0, st));
+        return QVL_OK;
+    }
+    return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, g_h, l_d, st);
 }
 
 static int check_attn_dims(const qvl_attn_dims *d) {
@@ -543,6 +558,7 @@ int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, flo
     if (!gate || !up || !q || !q_scales) return QVL_ERR_INVALID;
     if (M == 0) return QVL_OK;
     if (group_size == 0 || group_size % 16 || I % group_size) return QVL_ERR_INVALID;
+    if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(q, 8)) return QVL_ERR_INVALID;
     QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, q, q_scales, (int)M, (int)I, (int)group_size,
                                           (cudaStream_t)stream));
     return QVL_OK;

@@ -15,10 +15,15 @@
 // Tiling.  "Swap AB": the MMA's M dimension is 128 weight rows (TMEM lanes),
 // its N dimension a tile of NT activation rows (TMEM columns), K steps of 32
 // bytes.  A CTA computes a 128 x NT tile; one thread issues the TMA loads of
-// a 4-stage ring (128 B of K per stage, 128-byte swizzle), another thread
+// a stage ring (128 B of K per stage, 128-byte swizzle), another thread
 // issues the MMAs and commits each stage back to the ring, and four warps
-// read the accumulators (tcgen05.ld) for the epilogue.  Every wait is bounded.
+// read the accumulators (tcgen05.ld) for the epilogue, with the tile's
+// activation scales staged in shared memory beforehand.  Products of two or
+// more waves of tiles run on a persistent kernel with double-buffered
+// accumulators; smaller ones split K over a thread-block cluster.  Every wait
+// is bounded.
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <cooperative_groups.h>
 #include "tc_common.cuh"
@@ -53,6 +58,46 @@ struct TcSmem {
     static constexpr int kSt = NT >= 128 ? 2 : (NT >= 64 ? 3 : kStages);
     static constexpr int kBytes = kSt * kStage + 1024 /* align */ + 256 /* barriers */;
 };
+
+// Epilogue of one 128 x NT accumulator tile for the 32 weight rows of this
+// warp (TMEM lanes lane_off >> 16 ..+31; this thread: row n, weight scale ws).
+// as_s: the tile's NT activation scales, staged in shared memory before the
+// accumulators are waited for.  32 columns per tcgen05.wait::ld; in the
+// accumulate form the C values of a chunk are loaded before that wait.
+template <int NT>
+__device__ __forceinline__ void epilogue_rows(uint32_t d_hi, uint32_t d_lo, uint32_t lane_off,
+                                              const float *as_s, float ws, int n, int m0, int M, int N,
+                                              float *__restrict C, int acc) {
+    constexpr int kC = NT < 32 ? NT : 32;
+#pragma unroll 1
+    for (int c0 = 0; c0 < NT; c0 += kC) {
+        uint32_t hi[kC], lo[kC];
+#pragma unroll
+        for (int h = 0; h < kC; h += 16) {
+            tc::tmem_ld16(d_hi + lane_off + c0 + h, *reinterpret_cast<uint32_t(*)[16]>(hi + h));
+            tc::tmem_ld16(d_lo + lane_off + c0 + h, *reinterpret_cast<uint32_t(*)[16]>(lo + h));
+        }
+        float cv[kC];
+        if (acc) {
+#pragma unroll
+            for (int j = 0; j < kC; ++j) {
+                const int m = m0 + c0 + j;
+                cv[j] = (m < M && n < N) ? C[(size_t)m * N + n] : 0.0f;
+            }
+        }
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < kC; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < M && n < N) {
+                const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
+                const float p = mul_rn(__int2float_rn(S), as_s[c0 + j]);
+                const float v = fma_rn(p, ws, 0.0f);
+                C[(size_t)m * N + n] = acc ? add_rn(cv[j], v) : v;   // residual add (add_vector order)
+            }
+        }
+    }
+}
 
 // grid: (ceil(M/NT), ceil(N/128), SPLIT); block 128; with SPLIT > 1 the SPLIT
 // CTAs of a cluster (1, 1, SPLIT) each take K/SPLIT and their exact int32
@@ -158,38 +203,26 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
 
     // ---- epilogue: 4 warps, warp w owns TMEM lanes (weight rows) 32w..32w+31
     pdl_wait();   // activation scales and C belong to the stream order
+    __shared__ float as_s[NT];
+    for (int i = threadIdx.x; i < NT; i += kThreads) as_s[i] = (m0 + i < M) ? __ldg(a_scale + m0 + i) : 0.0f;
+    const int n_row = n0 + warp * 32 + lane;
+    const float ws_row = (n_row < N) ? __ldg(w_scale + n_row) : 0.0f;
+    __syncthreads();
     const bool acc_ok = tc::mbar_wait(accbar, 0, &g_gemm_tc_timeout);
     tc::tc_fence_after();
     if constexpr (SPLIT == 1) {
-        if (acc_ok) {
-            const int n = n0 + warp * 32 + lane;
-            const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
-            const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-#pragma unroll 1
-            for (int c0 = 0; c0 < NT; c0 += 16) {
-                uint32_t hi[16], lo[16];
-                tc::tmem_ld16(d_hi + lane_off + c0, hi);
-                tc::tmem_ld16(d_lo + lane_off + c0, lo);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = m0 + c0 + j;
-                    if (m < M && n < N) {
-                        const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
-                        const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
-                        const float v = fma_rn(p, ws, 0.0f);
-                        float *cp = C + (size_t)m * N + n;
-                        *cp = acc ? add_rn(*cp, v) : v;   // residual add (add_vector order)
-                    }
-                }
-            }
-        }
+        if (acc_ok)
+            epilogue_rows<NT>(d_hi, d_lo, (uint32_t)(warp * 32) << 16, as_s, ws_row, n_row, m0, M, N, C, acc);
     } else {
-        // partial integer sums of this K slice -> shared memory [128 rows][NT]
-        // (the stage ring is idle now), then rank r of the cluster adds the
-        // SPLIT partials of rows [r*128/SPLIT, (r+1)*128/SPLIT) and finishes them.
+        // partial integer sums of this K slice -> shared memory [NT][128 weight
+        // rows] (a warp writes 32 consecutive words: no bank conflicts; the
+        // stage ring is idle now), then rank r of the cluster adds the SPLIT
+        // partials of weight rows [r*128/SPLIT, (r+1)*128/SPLIT) and finishes
+        // them, consecutive threads on consecutive weight rows (contiguous
+        // distributed-shared-memory reads, coalesced C stores).
         namespace cg = cooperative_groups;
         cg::cluster_group cluster = cg::this_cluster();
+        static_assert(kBM * NT * 4 <= TcSmem<NT>::kSt * TcSmem<NT>::kStage, "partials exceed the stage ring");
         int32_t *part = reinterpret_cast<int32_t *>(smem);
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         const int row = warp * 32 + lane;
@@ -200,19 +233,19 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
             tc::tmem_ld16(d_lo + lane_off + c0, lo);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) part[row * NT + c0 + j] = acc_ok ? (int)(hi[j] * 256u + lo[j]) : 0;
+            for (int j = 0; j < 16; ++j) part[(c0 + j) * kBM + row] = acc_ok ? (int)(hi[j] * 256u + lo[j]) : 0;
         }
         cluster.sync();
         const int rank = (int)cluster.block_rank();
         constexpr int kRows = kBM / SPLIT;
         for (int e = threadIdx.x; e < kRows * NT; e += kThreads) {
-            const int r = rank * kRows + e / NT, j = e % NT;
+            const int r = rank * kRows + e % kRows, j = e / kRows;
             uint32_t S = 0;
 #pragma unroll
-            for (int k = 0; k < SPLIT; ++k) S += (uint32_t)cluster.map_shared_rank(part, k)[r * NT + j];
+            for (int k = 0; k < SPLIT; ++k) S += (uint32_t)cluster.map_shared_rank(part, k)[j * kBM + r];
             const int n = n0 + r, m = m0 + j;
             if (acc_ok && m < M && n < N) {
-                const float p = mul_rn(__int2float_rn((int)S), __ldg(a_scale + m));
+                const float p = mul_rn(__int2float_rn((int)S), as_s[j]);
                 const float v = fma_rn(p, __ldg(w_scale + n), 0.0f);
                 float *cp = C + (size_t)m * N + n;
                 *cp = acc ? add_rn(*cp, v) : v;
@@ -358,7 +391,11 @@ gemm_i8_tc_persistent(const __grid_constant__ CUtensorMap tm_w, const __grid_con
             }
         }
     } else {
-        // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31 = weight rows
+        // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31 = weight rows;
+        // each warp stages the tile's activation scales in its own as_s[.][b]
+        // (no block barrier, whose wait could not be bounded) before the
+        // accumulators are waited for
+        __shared__ float as_s[4][2][NT];
         pdl_wait();
         const int q4 = warp & 3;
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
@@ -366,31 +403,16 @@ gemm_i8_tc_persistent(const __grid_constant__ CUtensorMap tm_w, const __grid_con
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
             const int m0 = (t % mt) * NT, n0 = (t / mt) * kBM;
             const int b = i & 1, u = i >> 1;
+            for (int r = lane; r < NT; r += 32) as_s[q4][b][r] = (m0 + r < M) ? __ldg(a_scale + m0 + r) : 0.0f;
+            const int n = n0 + q4 * 32 + lane;
+            const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
+            __syncwarp();
             ok = tc::mbar_wait(tfull0 + 8 * b, u & 1, &g_gemm_tc_timeout);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc::tc_fence_after();
             const uint32_t d_hi = tmem + (uint32_t)(b * 2 * NT), d_lo = d_hi + NT;
-            const int n = n0 + q4 * 32 + lane;
-            const float ws = (n < N) ? __ldg(w_scale + n) : 0.0f;
-#pragma unroll 1
-            for (int c0 = 0; c0 < NT; c0 += 16) {
-                uint32_t hi[16], lo[16];
-                tc::tmem_ld16(d_hi + lane_off + c0, hi);
-                tc::tmem_ld16(d_lo + lane_off + c0, lo);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = m0 + c0 + j;
-                    if (m < M && n < N) {
-                        const int S = (int)(hi[j] * 256u + lo[j]);   // exact mod 2^32, |S| < 2^31
-                        const float p = mul_rn(__int2float_rn(S), __ldg(a_scale + m));
-                        const float v = fma_rn(p, ws, 0.0f);
-                        float *cp = C + (size_t)m * N + n;
-                        *cp = acc ? add_rn(*cp, v) : v;
-                    }
-                }
-            }
+            epilogue_rows<NT>(d_hi, d_lo, lane_off, as_s[q4][b], ws, n, m0, M, N, C, acc);
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cta(tempty0 + 8 * b);
@@ -480,6 +502,18 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
 }
 
 template <int NT>
+cudaError_t launch_split(int split, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
+                         const float *as, const float *ws, float *C, int M, int N, int K, int acc,
+                         cudaStream_t st) {
+    switch (split) {
+        case 8: return launch_nt<NT, 8>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
+        case 4: return launch_nt<NT, 4>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
+        case 2: return launch_nt<NT, 2>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
+        default: return launch_nt<NT, 1>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
+    }
+}
+
+template <int NT>
 cudaError_t launch_persistent(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
                               const float *ws, float *C, int M, int N, int K, int acc, cudaStream_t st) {
     auto kern = gemm_i8_tc_persistent<NT>;
@@ -544,33 +578,23 @@ cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M,
 cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
                                      const float *ws, float *C, int M, int N, int K, int acc,
                                      cudaStream_t stream) {
-    // the widest activation tile that still gives ~one CTA per SM: narrower
-    // tiles (and, at 32 rows, split-K) for small-N products such as the k / v
-    // projections of a prompt
-    const long nt128 = (long)((N + kBM - 1) / kBM) * ((M + 127) / 128);
-    const long nt64 = (long)((N + kBM - 1) / kBM) * ((M + 63) / 64);
-    const int NT = M >= 512 ? 128
-                   : (M >= 256 && nt128 >= 148) ? 128
-                   : (M >= 64 && nt64 >= 148) ? 64 : 32;
+    // Activation tile: 128 rows from M >= 256 (64 from 64, else 32).  Products
+    // of two or more waves of 128 x 128 tiles run on the persistent kernel;
+    // smaller ones split K over a cluster until there are ~2 CTAs per SM
+    // (exact int32 partial sums, added through distributed shared memory).
+    const int NT = M >= 256 ? 128 : (M >= 64 ? 64 : 32);
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
         return cudaErrorInvalidValue;
-    if (NT == 128) {
-        // many tiles: the persistent kernel (double-buffered accumulators)
-        if (persist_enabled() && (long)((M + 127) / 128) * ((N + kBM - 1) / kBM) >= 2 * 148)
-            return launch_persistent<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-        return launch_nt<128, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    }
-    if (NT == 64) return launch_nt<64, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    // small M (decode batches): split K over a cluster until ~2 CTAs per SM
-    const long tiles = (long)((N + kBM - 1) / kBM) * ((M + 31) / 32);
+    const long tiles = (long)((N + kBM - 1) / kBM) * ((M + NT - 1) / NT);
+    if (NT == 128 && tiles >= 2 * 148 && persist_enabled())
+        return launch_persistent<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
     const int nkb = K / kBK;
     int split = 1;
     while (split < 8 && tiles * split * 2 <= 2 * 148 && nkb % (split * 2) == 0) split *= 2;
-    if (split == 8) return launch_nt<32, 8>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    if (split == 4) return launch_nt<32, 4>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    if (split == 2) return launch_nt<32, 2>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    return launch_nt<32, 1>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 128) return launch_split<128>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 64) return launch_split<64>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    return launch_split<32>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
 }
 
 cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,

@@ -19,7 +19,8 @@ namespace qvl {
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const float *__restrict x,
                                                             int16_t *__restrict q,
                                                             float *__restrict s, int K, int g,
-                                                            int gpb) {
+                                                            int gpb, int8_t *__restrict hi,
+                                                            uint8_t *__restrict lo) {
     extern __shared__ __align__(16) float xs[];
     __shared__ float inv_s[16];
     pdl_launch_dependents();
@@ -33,20 +34,12 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float *__restr
     for (int i = threadIdx.x; i < n / 4; i += blockDim.x)
         reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(x + base)[i];
     __syncthreads();
-    const int hw = threadIdx.x >> 4;
-    const bool active = hw < ng;        // whole half-warps only: keep them in the shuffles
-    const int gl = active ? hw : 0;
-    const float sc = group_scale_ref(xs + (size_t)gl * g, g, threadIdx.x & 15);
-    if (active && (threadIdx.x & 15) == 0) {
-        s[(size_t)row * G + g0 + gl] = sc;
-        inv_s[gl] = __fdiv_rn(1.0f, sc);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) q[base + i] = quant_one(xs[i], inv_s[i / g]);
+    quantize_slice(xs, g, ng, q + base, s + (size_t)row * G + g0, hi ? hi + base : nullptr,
+                   lo ? lo + base : nullptr, inv_s);
 }
 
 cudaError_t launch_quantize_rows(const float *x, int16_t *q, float *s, int M, int K, int g,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, int8_t *hi, uint8_t *lo) {
     const int G = K / g;
     int gpb = 8192 / g;
     gpb = gpb < 1 ? 1 : (gpb > 16 ? 16 : gpb);
@@ -66,7 +59,7 @@ cudaError_t launch_quantize_rows(const float *x, int16_t *q, float *s, int M, in
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, q, s, K, g, gpb);
+    return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, q, s, K, g, gpb, hi, lo);
 }
 
 }  // namespace qvl

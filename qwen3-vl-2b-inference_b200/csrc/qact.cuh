@@ -4,8 +4,10 @@
 #include "common.cuh"
 
 namespace qvl {
+// hi/lo (optional, both or neither): the tensor-core GEMM's activation
+// planes q >> 8 (int8) and q & 255 (uint8), [M, K] each, written alongside q.
 cudaError_t launch_quantize_rows(const float *x, int16_t *q, float *s, int M, int K, int g,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, int8_t *hi = nullptr, uint8_t *lo = nullptr);
 
 __device__ __forceinline__ float inv127() { return __int_as_float(0x3c010204); }  // (float)1/127
 
@@ -69,6 +71,37 @@ __device__ __forceinline__ float group_scale_ref(const float *xg, int g, int t16
     float ss = group_sumsq_ref(xg, g, t16);
     float inv_g = __fdiv_rn(1.0f, (float)g);
     return mul_rn(__fsqrt_rn(fma_rn(ss, inv_g, 1e-6f)), inv127());
+}
+
+// Scales and quantisation of a block's slice xs[0, ng * g) of one row, held in
+// shared memory (ng <= 16 groups, block of 256 threads): half-warp h < ng runs
+// group h's scale chain -- warps with no live group skip it -- then all
+// threads quantise four elements at a time.  s, q, hi, lo point at the
+// slice's first scale / element; hi and lo may be null.
+__device__ __forceinline__ void quantize_slice(const float *xs, int g, int ng, int16_t *q, float *s,
+                                               int8_t *hi, uint8_t *lo, float *inv_s) {
+    const int hw = threadIdx.x >> 4;
+    if ((threadIdx.x >> 5) * 2 < ng) {
+        const int gl = hw < ng ? hw : 0;   // a dead half of a live warp repeats group 0 (shuffle partners)
+        const float sc = group_scale_ref(xs + (size_t)gl * g, g, threadIdx.x & 15);
+        if (hw < ng && (threadIdx.x & 15) == 0) {
+            s[gl] = sc;
+            inv_s[gl] = __fdiv_rn(1.0f, sc);
+        }
+    }
+    __syncthreads();
+    const int n4 = ng * g / 4;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = reinterpret_cast<const float4 *>(xs)[i];
+        const float inv = inv_s[ng == 1 ? 0 : (4 * i) / g];
+        const uint32_t a = (uint16_t)quant_one(v.x, inv), b = (uint16_t)quant_one(v.y, inv);
+        const uint32_t c = (uint16_t)quant_one(v.z, inv), d = (uint16_t)quant_one(v.w, inv);
+        reinterpret_cast<uint2 *>(q)[i] = make_uint2(a | (b << 16), c | (d << 16));
+        if (hi) {
+            reinterpret_cast<uint32_t *>(hi)[i] = (a >> 8) | ((b >> 8) << 8) | ((c >> 8) << 16) | ((d >> 8) << 24);
+            reinterpret_cast<uint32_t *>(lo)[i] = (a & 255u) | ((b & 255u) << 8) | ((c & 255u) << 16) | (d << 24);
+        }
+    }
 }
 
 }  // namespace qvl

@@ -39,18 +39,14 @@ swiglu_quant_kernel(const float *__restrict gate, const float *__restrict up,
     const int row = blockIdx.y;
     const size_t base = (size_t)row * I + (size_t)g0 * g;
     const int n = ng * g;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) hs[i] = swiglu_one(gate[base + i], up[base + i]);
-    __syncthreads();
-    const int hw = threadIdx.x >> 4;
-    const bool active = hw < ng;        // whole half-warps only: keep them in the shuffles
-    const int gl = active ? hw : 0;
-    const float sc = group_scale_ref(hs + (size_t)gl * g, g, threadIdx.x & 15);
-    if (active && (threadIdx.x & 15) == 0) {
-        s[(size_t)row * G + g0 + gl] = sc;
-        inv_s[gl] = __fdiv_rn(1.0f, sc);
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+        const float4 a = reinterpret_cast<const float4 *>(gate + base)[i];
+        const float4 b = reinterpret_cast<const float4 *>(up + base)[i];
+        reinterpret_cast<float4 *>(hs)[i] = make_float4(swiglu_one(a.x, b.x), swiglu_one(a.y, b.y),
+                                                        swiglu_one(a.z, b.z), swiglu_one(a.w, b.w));
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) q[base + i] = quant_one(hs[i], inv_s[i / g]);
+    quantize_slice(hs, g, ng, q + base, s + (size_t)row * G + g0, nullptr, nullptr, inv_s);
 }
 
 __global__ void expf_host_kernel(const float *__restrict x, float *__restrict y, long n) {
