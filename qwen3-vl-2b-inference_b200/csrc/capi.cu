@@ -173,7 +173,8 @@ int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales, size_t M, siz
 size_t qvl_linear_i8_workspace_bytes(size_t M, size_t K, size_t group_size) {
     if (group_size == 0 || K % group_size) return 0;
     size_t b = qbuf_bytes(M, K, group_size);
-    if (M >= 16 && group_size == K && K % 128 == 0) b += qvl::gemm_tc_planes_bytes(M, K);
+    if (M >= 16 && K % 128 == 0 && (group_size == K || qvl::gemm_tc_grouped_size(group_size, K)))
+        b += qvl::gemm_tc_planes_bytes(M, K);
     return b;
 }
 
@@ -223,7 +224,8 @@ int qvl_linear_i8(const float *A, const int8_t *B, const float *B_scales, float 
         int8_t *hi = reinterpret_cast<int8_t *>(static_cast<char *>(workspace) + need);
         uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + qvl::gemm_tc_planes_bytes(M, K) / 2;
         QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st, hi, lo));
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo, qs, B, B_scales, C, (int)M, (int)N, (int)K, 0, st));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo, qs, B, B_scales, C, (int)M, (int)N, (int)K, 0, st,
+                                                   (int)g));
         return QVL_OK;
     }
     QVL_CUDA_TRY(qvl::launch_quantize_rows(A, q, qs, (int)M, (int)K, (int)g, st));
@@ -460,8 +462,10 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
     QVL_CUDA_TRY(qvl::launch_quantize_rows(x, qx, qxs, (int)M, (int)H, (int)g_in, st, tc_gu ? hi : nullptr,
                                            tc_gu ? lo_gu : nullptr));
     if (tc_gu) {
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wg, sg, gate, (int)M, (int)I, (int)H, 0, st));
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wu, su, up, (int)M, (int)I, (int)H, 0, st));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wg, sg, gate, (int)M, (int)I, (int)H, 0, st,
+                                                   (int)g_in));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_gu, qxs, Wu, su, up, (int)M, (int)I, (int)H, 0, st,
+                                                   (int)g_in));
     } else {
         rc = run_q16_linear(qx, qxs, Wg, sg, gate, M, I, H, g_in, l_gu, st);
         if (!rc) rc = run_q16_linear(qx, qxs, Wu, su, up, M, I, H, g_in, l_gu, st);
@@ -477,7 +481,8 @@ int qvl_swiglu_mlp_i8(const float *x, const int8_t *Wg, const float *sg, const i
         QVL_CUDA_TRY(qvl::launch_swiglu_quant(gate, up, qh, qhs, (int)M, (int)I, (int)g_h, st));
     }
     if (tc_d) {
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_d, qhs, Wd, sd, out, (int)M, (int)H, (int)I, 0, st));
+        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo_d, qhs, Wd, sd, out, (int)M, (int)H, (int)I, 0, st,
+                                                   (int)g_h));
         return QVL_OK;
     }
     return run_q16_linear(qh, qhs, Wd, sd, out, M, H, I, g_h, l_d, st);

@@ -423,6 +423,213 @@ gemm_i8_tc_persistent(const __grid_constant__ CUtensorMap tm_w, const __grid_con
     if (warp == 1) tc::tmem_dealloc(tmem, kCols);
 }
 
+// Group-wise weight scales (g in {32, 64} or a multiple of 128, g < K): the
+// reference's M > 1 order per output is acc = fma(float(S_g) * a_s[m, g],
+// w_s[n, g], acc) over the groups in ascending order, S_g the exact integer
+// sum of group g.  A "unit" is what one accumulator set holds: one group when
+// g >= 128 (g / 128 stages of K), else the GPK = 128 / g groups of one stage.
+// Each unit's hi/lo sums go to their own TMEM columns (GPK x 2 x NT per
+// buffer, two buffers); eight epilogue warps (two per TMEM lane quarter, each
+// taking half of the tile's columns) drain every unit as soon as it is
+// complete and keep the fp32 chains in registers, so the integer sums of unit
+// u+1 run on the tensor cores while unit u is scaled.  Persistent over tiles
+// like gemm_i8_tc_persistent; every wait is bounded, no block barrier inside
+// the loops.
+constexpr int kGroupedThreads = 320;   // producer, MMA, 8 epilogue warps
+template <int NT>
+struct TcGroupedSmem {
+    static constexpr int kA = kBM * kBK;
+    static constexpr int kB = NT * kBK;
+    static constexpr int kStage = kA + 2 * kB;
+    static constexpr int kSt = (192 * 1024) / kStage;
+    static constexpr int kBytes = kSt * kStage + 1024 + 256;
+};
+
+template <int NT, int GPK>
+__global__ void __launch_bounds__(kGroupedThreads, 1)
+gemm_i8_tc_grouped(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
+                   const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
+                   const float *__restrict w_scale, float *__restrict C, int M, int N, int K, int g, int acc) {
+    static_assert(GPK * NT <= 128 && (GPK == 1 || GPK == 2 || GPK == 4), "unit exceeds 256 TMEM columns");
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    using L = TcGroupedSmem<NT>;
+    constexpr int kS = L::kSt;
+    constexpr int kHalf = NT / 2;                       // columns per epilogue warp
+    constexpr uint32_t kBuf = GPK * 2 * NT;             // TMEM columns per unit buffer
+    constexpr uint32_t kCols = 2 * kBuf < 32 ? 32 : 2 * kBuf;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kS * L::kStage);
+    const uint32_t full0 = tc::smem_u32(bars);
+    const uint32_t empty0 = tc::smem_u32(bars + kS);
+    const uint32_t tfull0 = tc::smem_u32(bars + 2 * kS);
+    const uint32_t tempty0 = tc::smem_u32(bars + 2 * kS + 2);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kS + 4);
+    __shared__ int timed_out_at_entry;
+    __shared__ float as_w[8][GPK * kHalf];              // per epilogue warp: this unit's activation scales
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (M + NT - 1) / NT, ntl = (N + kBM - 1) / kBM;
+    const int tiles = mt * ntl;
+    const int G = K / g;
+    const int units = G / GPK;                         // per tile
+    const int kpu = GPK == 1 ? g / kBK : 1;            // stages per unit
+
+    if (threadIdx.x == 0) {
+        timed_out_at_entry = *reinterpret_cast<volatile int *>(&g_gemm_tc_timeout) != 0;
+        for (int i = 0; i < kS; ++i) {
+            tc::mbar_init(full0 + 8 * i, 1);
+            tc::mbar_init(empty0 + 8 * i, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(tfull0 + 8 * b, 1);
+            tc::mbar_init(tempty0 + 8 * b, 8);    // one elected lane per epilogue warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        tc::prefetch_tmap(&tm_w);
+        tc::prefetch_tmap(&tm_hi);
+        tc::prefetch_tmap(&tm_lo);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
+    bool ok = !timed_out_at_entry;
+    const int nk = K / kBK;
+
+    if (warp == 0) {
+        if (lane == 0 && ok) {
+            int kk = 0, issued = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % mt) * NT, n0 = (t / mt) * kBM;
+                for (int kb = 0; kb < nk && ok; ++kb, ++kk) {
+                    const int s = kk % kS;
+                    if (kk >= kS) ok = tc::mbar_wait(empty0 + 8 * s, ((kk / kS) - 1) & 1, &g_gemm_tc_timeout);
+                    if (!ok) break;
+                    unsigned char *st = smem + s * L::kStage;
+                    tc::mbar_expect_tx(full0 + 8 * s, L::kStage);
+                    tc::tma_load_2d(tc::smem_u32(st), &tm_w, kb * kBK, n0, full0 + 8 * s);
+                    if (kk == 0) pdl_wait();
+                    tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, kb * kBK, m0, full0 + 8 * s);
+                    tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, kb * kBK, m0, full0 + 8 * s);
+                    issued = kk + 1;
+                }
+            }
+            if (!ok)
+                for (int k2 = issued - 1; k2 >= 0 && k2 >= issued - kS; --k2)
+                    tc::mbar_wait(full0 + 8 * (k2 % kS), (k2 / kS) & 1, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && ok) {
+            constexpr uint32_t id_hi = tc::idesc_i8(kBM, NT, true);
+            constexpr uint32_t id_lo = tc::idesc_i8(kBM, NT, false);
+            constexpr int kPerGroup = (kBK / kUmmaK) / GPK;   // MMA K steps per group inside a stage
+            int kk = 0, u = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                for (int uu = 0; uu < units && ok; ++uu, ++u) {
+                    const int b = u & 1;
+                    if (u >= 2) ok = tc::mbar_wait(tempty0 + 8 * b, ((u >> 1) - 1) & 1, &g_gemm_tc_timeout);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint32_t dbase = tmem + (uint32_t)b * kBuf;
+                    for (int kq = 0; kq < kpu && ok; ++kq, ++kk) {
+                        const int s = kk % kS;
+                        ok = tc::mbar_wait(full0 + 8 * s, (kk / kS) & 1, &g_gemm_tc_timeout);
+                        if (!ok) break;
+                        tc::tc_fence_after();
+                        const uint32_t a_base = tc::smem_u32(smem + s * L::kStage);
+                        const uint32_t h_base = a_base + L::kA;
+                        const uint32_t l_base = h_base + L::kB;
+#pragma unroll
+                        for (int k = 0; k < kBK / kUmmaK; ++k) {
+                            const int gk = k / kPerGroup;
+                            const uint32_t d_hi = dbase + (uint32_t)(gk * 2 * NT), d_lo = d_hi + NT;
+                            const uint32_t accum = GPK == 1 ? ((kq > 0 || k > 0) ? 1u : 0u)
+                                                            : ((k % kPerGroup) != 0 ? 1u : 0u);
+                            const uint64_t ad = tc::sdesc_k_sw128(a_base + k * kUmmaK);
+                            tc::mma_i8(d_hi, ad, tc::sdesc_k_sw128(h_base + k * kUmmaK), id_hi, accum);
+                            tc::mma_i8(d_lo, ad, tc::sdesc_k_sw128(l_base + k * kUmmaK), id_lo, accum);
+                        }
+                        tc::tc_commit(empty0 + 8 * s);
+                    }
+                    if (ok) tc::tc_commit(tfull0 + 8 * b);
+                }
+            }
+        }
+    } else {
+        // epilogue warps 2..9: TMEM lane quarter warp % 4, column half (warp - 2) / 4
+        pdl_wait();
+        const int we = warp - 2, q4 = warp & 3, h = we >> 2;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        float *asw = as_w[we];
+        int u = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const int m0 = (t % mt) * NT, n0 = (t / mt) * kBM;
+            const int n = n0 + q4 * 32 + lane;
+            const int mc = m0 + h * kHalf;                 // this warp's first column
+            float accv[kHalf];
+#pragma unroll
+            for (int j = 0; j < kHalf; ++j) accv[j] = 0.0f;
+            for (int uu = 0; uu < units && ok; ++uu, ++u) {
+                const int b = u & 1;
+                // this unit's scales: a_s[m, gi] for the warp's columns, w_s[n, gi]
+                __syncwarp();
+                for (int e = lane; e < GPK * kHalf; e += 32) {
+                    const int gk = e / kHalf, m = mc + e % kHalf;
+                    asw[e] = m < M ? __ldg(a_scale + (size_t)m * G + uu * GPK + gk) : 0.0f;
+                }
+                float wsg[GPK];
+#pragma unroll
+                for (int gk = 0; gk < GPK; ++gk) wsg[gk] = n < N ? __ldg(w_scale + (size_t)n * G + uu * GPK + gk) : 0.0f;
+                __syncwarp();
+                ok = tc::mbar_wait(tfull0 + 8 * b, (u >> 1) & 1, &g_gemm_tc_timeout);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc::tc_fence_after();
+#pragma unroll
+                for (int gk = 0; gk < GPK; ++gk) {
+                    const uint32_t dh = tmem + (uint32_t)b * kBuf + (uint32_t)(gk * 2 * NT + h * kHalf) + lane_off;
+#pragma unroll
+                    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+                        uint32_t hi[16], lo[16];
+                        tc::tmem_ld16(dh + c0, hi);
+                        tc::tmem_ld16(dh + NT + c0, lo);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int S = (int)(hi[j] * 256u + lo[j]);
+                            const float p = mul_rn(__int2float_rn(S), asw[gk * kHalf + c0 + j]);
+                            accv[c0 + j] = fma_rn(p, wsg[gk], accv[c0 + j]);
+                        }
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cta(tempty0 + 8 * b);
+            }
+            if (!ok) break;
+            if (n < N) {
+#pragma unroll
+                for (int j = 0; j < kHalf; ++j) {
+                    const int m = mc + j;
+                    if (m < M) {
+                        float *cp = C + (size_t)m * N + n;
+                        *cp = acc ? add_rn(*cp, accv[j]) : accv[j];
+                    }
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, kCols);
+}
+
 // q int16 [M, K] -> hi int8 [M, K] (q >> 8), lo uint8 [M, K] (q & 255).
 __global__ void split_hi_lo_kernel(const int16_t *__restrict q, int8_t *__restrict hi, uint8_t *__restrict lo,
                                    long n) {
@@ -536,6 +743,29 @@ cudaError_t launch_persistent(const CUtensorMap &mw, const CUtensorMap &mh, cons
     return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
 }
 
+template <int NT, int GPK>
+cudaError_t launch_grouped(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
+                           const float *ws, float *C, int M, int N, int K, int g, int acc, cudaStream_t st) {
+    auto kern = gemm_i8_tc_grouped<NT, GPK>;
+    const int smem = TcGroupedSmem<NT>::kBytes;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long tiles = (long)((M + NT - 1) / NT) * ((N + kBM - 1) / kBM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles < sms ? tiles : sms));
+    cfg.blockDim = dim3(kGroupedThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, g, acc);
+}
+
 }  // namespace
 
 int *gemm_tc_timeout_word() {
@@ -554,8 +784,12 @@ static bool persist_enabled() {
     return v != 0;
 }
 
+bool gemm_tc_grouped_size(size_t g, size_t K) {
+    return g < K && (g == 32 || g == 64 || (g % kBK == 0 && K % g == 0));
+}
+
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g) {
-    return M >= 16 && g == K && K % kBK == 0 && N >= kBM && (N + kBM - 1) / kBM <= 65535 && get_encode() != nullptr;
+    return M >= 16 && (g == K || gemm_tc_grouped_size(g, K)) && K % kBK == 0 && N >= kBM && (N + kBM - 1) / kBM <= 65535 && get_encode() != nullptr;
 }
 
 size_t gemm_tc_planes_bytes(size_t M, size_t K) { return 2 * ((M * K + 255) & ~(size_t)255); }
@@ -577,7 +811,28 @@ cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M,
 
 cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
                                      const float *ws, float *C, int M, int N, int K, int acc,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, int g) {
+    if (g != 0 && g != K) {
+        // group-wise scales: groups per stage GPK = 128 / g (1 from g = 128);
+        // the widest activation tile that fits the unit's TMEM columns,
+        // narrowed while the tiles would not cover the GPU
+        const int gpk = g >= kBK ? 1 : kBK / g;
+        int NT = 128 / gpk;
+        while (NT > 32 && (long)((M + NT - 1) / NT) * ((N + kBM - 1) / kBM) < 148) NT /= 2;
+        CUtensorMap mw, mh, ml;
+        if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
+            return cudaErrorInvalidValue;
+        if (gpk == 1) {
+            if (NT == 128) return launch_grouped<128, 1>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+            if (NT == 64) return launch_grouped<64, 1>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+            return launch_grouped<32, 1>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+        }
+        if (gpk == 2) {
+            if (NT == 64) return launch_grouped<64, 2>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+            return launch_grouped<32, 2>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+        }
+        return launch_grouped<32, 4>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
+    }
     // Activation tile: 128 rows from M >= 256 (64 from 64, else 32).  Products
     // of two or more waves of 128 x 128 tiles run on the persistent kernel;
     // smaller ones split K over a cluster until there are ~2 CTAs per SM

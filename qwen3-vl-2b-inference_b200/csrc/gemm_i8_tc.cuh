@@ -5,8 +5,11 @@
 
 namespace qvl {
 // Tensor-core (tcgen05 kind::i8) INT8 GEMM with TILED summation semantics.
-// TILED summation, per-output-row weight scales (g == K), K % 128 == 0, M >= 16.
+// TILED summation, K % 128 == 0, M >= 16; per-output-row weight scales
+// (g == K) or group-wise ones with g in {32, 64} or a multiple of 128.
 bool gemm_tc_supported(size_t M, size_t N, size_t K, size_t g);
+// group sizes (g < K) the group-wise tensor-core kernel takes
+bool gemm_tc_grouped_size(size_t g, size_t K);
 // device address (current device) of the kernel's timeout word, or nullptr
 int *gemm_tc_timeout_word();
 // bytes of the hi/lo activation planes the GEMM needs in the caller's workspace
@@ -18,5 +21,5 @@ cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uin
 cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M, int K, cudaStream_t stream);
 cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
                                      const float *ws, float *C, int M, int N, int K, int acc,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, int g = 0);   // g: group size, 0 = K
 }  // namespace qvl

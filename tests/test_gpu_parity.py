@@ -191,7 +191,7 @@ def test_swiglu_matches(qvl, cuda):
     np.testing.assert_array_equal(out, ref)
 
 
-@pytest.mark.parametrize("M,g", [(1, 2048), (1, 128), (4, 2048), (64, 2048)])
+@pytest.mark.parametrize("M,g", [(1, 2048), (1, 128), (4, 2048), (64, 2048), (64, 128), (32, 64)])
 def test_swiglu_mlp(qvl, cuda, M, g):
     H, I = 2048, 6144
     rng = np.random.default_rng(50 + M)
@@ -340,6 +340,19 @@ def test_linear_prefill_tensor_core_bit_exact(qvl, cuda, M, N, K):
     x, w, ws = make_linear_inputs(7 * M + N, M, N, K, K)
     y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=False)
     np.testing.assert_array_equal(y.cpu().numpy(), oracle.linear_i8(x, w, ws, K, oracle.TILED, threads=16))
+
+
+@pytest.mark.parametrize("M,N,K,g", [(16, 256, 1024, 32), (48, 2048, 2048, 64), (64, 2048, 2048, 128),
+                                     (130, 1024, 2048, 64), (77, 300, 1024, 256), (200, 512, 2048, 512),
+                                     (512, 2048, 2048, 128), (512, 6144, 2048, 128), (452, 2048, 6144, 128),
+                                     (512, 1024, 2048, 32), (256, 2048, 2048, 64)])
+def test_linear_grouped_tensor_core_bit_exact(qvl, cuda, M, N, K, g):
+    """Group-wise scales at M >= 16 run the group-wise tcgen05 kernel: exact
+    integer sums per group, acc = fma(float(S) * a_s, w_s, acc) over the
+    groups in order (TILED), bit-exact with the oracle; ragged M and N."""
+    x, w, ws = make_linear_inputs(11 * M + N + g, M, N, K, g)
+    y = qvl.linear(dev(x, cuda), dev(w, cuda), dev(ws, cuda), group_quantized=True, group_size=g)
+    np.testing.assert_array_equal(y.cpu().numpy(), oracle.linear_i8(x, w, ws, g, oracle.TILED, threads=16))
 
 
 def test_linear_persistent_tensor_core_accumulate(qvl, cuda):
