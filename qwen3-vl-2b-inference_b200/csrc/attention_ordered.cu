@@ -34,64 +34,6 @@ __device__ __forceinline__ size_t kv_index(const int32_t *pt_row, int t, int kvh
 }
 }  // namespace
 
-// grid (ceil(max_ctx / 128), NKV, nq); block 128; smem kv_mul * 128 floats.
-__global__ void __launch_bounds__(kThreads)
-attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict k_pages,
-                           const int32_t *__restrict page_table, const int32_t *__restrict seq_ids,
-                           const int32_t *__restrict positions, float *__restrict scores, int max_ctx, int NH,
-                           int NKV, int P, int maxp) {
-    extern __shared__ float qs[];
-    pdl_launch_dependents();
-    pdl_wait();
-    const int i = blockIdx.z, kvh = blockIdx.y;
-    const int kvm = NH / NKV;
-    const int pos = positions[i];
-    for (int e = threadIdx.x; e < kvm * kD; e += blockDim.x) qs[e] = q[((size_t)i * NH + kvh * kvm) * kD + e];
-    __syncthreads();
-    const int t = blockIdx.x * kThreads + threadIdx.x;
-    if (pos < 0 || pos >= max_ctx || t > pos) return;
-    const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
-    const uint4 *kr = reinterpret_cast<const uint4 *>(k_pages + kv_index(pt_row, t, kvh, NKV, P));
-    float k[kD];
-#pragma unroll
-    for (int c = 0; c < kD / 8; ++c) {
-        const uint4 v = __ldg(kr + c);
-        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            k[8 * c + 2 * j] = f.x;
-            k[8 * c + 2 * j + 1] = f.y;
-        }
-    }
-    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)kD));
-    const bool tail = t >= (pos / 8) * 8;
-    for (int hh = 0; hh < kvm; ++hh) {
-        const float *qh = qs + hh * kD;
-        float l8[8];
-#pragma unroll
-        for (int l = 0; l < 8; ++l) l8[l] = 0.0f;
-        float r;
-        if (!tail) {
-#pragma unroll
-            for (int c = 0; c < kD; c += 8)
-#pragma unroll
-                for (int l = 0; l < 8; ++l) l8[l] = fma_rn(qh[c + l], k[c + l], l8[l]);
-            r = reduce8_ref(l8);
-        } else {
-#pragma unroll
-            for (int c = 0; c < kD; c += 8)
-#pragma unroll
-                for (int l = 0; l < 8; ++l) l8[l] = add_rn(l8[l], mul_rn(qh[c + l], k[c + l]));
-            r = l8[0];
-#pragma unroll
-            for (int l = 1; l < 8; ++l) r = add_rn(r, l8[l]);
-            r = add_rn(0.0f, r);
-        }
-        scores[((size_t)i * NH + kvh * kvm + hh) * max_ctx + t] = mul_rn(r, inv_sqrt_d);
-    }
-}
-
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem)),
                  "l"(gmem)
@@ -101,104 +43,221 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-constexpr int kSumChunk = 2048;    // exponentials staged per pass of the lane sums
-constexpr int kPvChunk = 64;       // V rows staged per P.V step (16 KB), double-buffered
+constexpr int kKRow = kD * 2 + 16;     // staged key row: 256 B + 16 B of padding (no bank conflicts)
 
-// grid (NH, nq); block 128 (thread = output dimension d).  `scores` rows are
-// overwritten with the exponentials.  Everything read sequentially (the lane
-// sums, the P.V chains) comes from shared memory: the exponentials in chunks
-// of 2048, the V rows in double-buffered chunks of 64 fetched with cp.async.
+// grid (ceil(max_ctx / 128), NKV, nq); block 128; dynamic smem: the KV
+// head's query rows (kv_mul * 128 floats), then the block's 128 key rows.
+// The key rows are staged with contiguous 16-byte cp.async copies (16
+// threads per row) and each thread then reads its own row from shared memory.
+template <int KVM>
 __global__ void __launch_bounds__(kThreads)
+attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict k_pages,
+                           const int32_t *__restrict page_table, const int32_t *__restrict seq_ids,
+                           const int32_t *__restrict positions, float *__restrict scores, int max_ctx, int NH,
+                           int NKV, int P, int maxp) {
+    extern __shared__ __align__(16) float qs[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int i = blockIdx.z, kvh = blockIdx.y;
+    constexpr int kvm = KVM;
+    const int pos = positions[i];
+    const int t0 = blockIdx.x * kThreads;
+    if (pos < 0 || pos >= max_ctx || t0 > pos) return;
+    unsigned char *ks = reinterpret_cast<unsigned char *>(qs + kvm * kD);
+    const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
+    const int rows = min(kThreads, pos + 1 - t0);
+    for (int e = threadIdx.x; e < rows * 16; e += kThreads) {
+        const int r = e >> 4, c = e & 15;
+        cp_async16(ks + r * kKRow + c * 16,
+                   reinterpret_cast<const uint4 *>(k_pages + kv_index(pt_row, t0 + r, kvh, NKV, P)) + c);
+    }
+    cp_async_commit();
+    for (int e = threadIdx.x; e < kvm * kD; e += blockDim.x) qs[e] = q[((size_t)i * NH + kvh * kvm) * kD + e];
+    cp_async_wait<0>();
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t > pos) return;
+    const uint4 *kr = reinterpret_cast<const uint4 *>(ks + threadIdx.x * kKRow);
+    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)kD));
+    const bool tail = t >= (pos / 8) * 8;
+    // the KVM heads' 8-lane chains advance together, 8 key values at a time
+    // (each head's chain in its own order: lane l over d = l, l+8, ...)
+    float l8[KVM][8];
+#pragma unroll
+    for (int hh = 0; hh < KVM; ++hh)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) l8[hh][l] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kD / 8; ++c) {
+        const uint4 v = kr[c];
+        const __half2 *hv = reinterpret_cast<const __half2 *>(&v);
+        float kc[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(hv[j]);
+            kc[2 * j] = f.x;
+            kc[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int hh = 0; hh < KVM; ++hh) {
+            const float *qv = qs + hh * kD + 8 * c;
+            if (!tail) {
+#pragma unroll
+                for (int l = 0; l < 8; ++l) l8[hh][l] = fma_rn(qv[l], kc[l], l8[hh][l]);
+            } else {
+#pragma unroll
+                for (int l = 0; l < 8; ++l) l8[hh][l] = add_rn(l8[hh][l], mul_rn(qv[l], kc[l]));
+            }
+        }
+    }
+#pragma unroll
+    for (int hh = 0; hh < KVM; ++hh) {
+        float r;
+        if (!tail) {
+            r = reduce8_ref(l8[hh]);
+        } else {
+            r = l8[hh][0];
+#pragma unroll
+            for (int l = 1; l < 8; ++l) r = add_rn(r, l8[hh][l]);
+            r = add_rn(0.0f, r);
+        }
+        scores[((size_t)i * NH + kvh * KVM + hh) * max_ctx + t] = mul_rn(r, inv_sqrt_d);
+    }
+}
+
+constexpr int kSumChunk = 1024;    // exponentials staged per pass of the lane sums (per query head)
+constexpr int kPvChunk = 64;       // V rows per P.V stage (16 KB)
+constexpr int kPvStages = 4;       // stages in flight (cp.async ring)
+
+template <int KVM>
+struct PvSmem {
+    static constexpr size_t kV = (size_t)kPvStages * kPvChunk * kD * 2;        // fp16 V rows
+    static constexpr size_t kP = (size_t)kPvStages * KVM * kPvChunk * 4;       // probabilities (global path)
+    static constexpr size_t kE = (size_t)KVM * kSumChunk * 4;                  // exponentials staged for the sums
+    static constexpr size_t kBytes = kV + kP + kE;
+};
+// Contexts up to this many positions keep the whole score row of each query
+// head in shared memory (KVM * 4 B per position).
+constexpr int kSmemCtx = 4096;
+
+// grid (NKV, nq); block KVM * 128: the KVM query heads that share a KV head,
+// thread (hh, d) = output dimension d of query head kvh * KVM + hh.  Each
+// head's 128 threads form its softmax in the reference's order (maximum,
+// exponentials, 8 float lane sums t-ascending, the lanes and the tail in
+// double, p = e * (float)(1 / sum)); then every V row is staged once for all
+// KVM heads through a 4-stage cp.async ring and each thread runs its fma
+// chain over t ascending.  SE: the row (n <= kSmemCtx) lives in shared
+// memory from the first read on; otherwise the exponentials are formed in
+// place in `scores` and staged in chunks.
+template <int KVM, bool SE>
+__global__ void __launch_bounds__(KVM * kThreads)
 attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
                                const int32_t *__restrict seq_ids, const int32_t *__restrict positions,
                                float *__restrict scores, float *__restrict out, int max_ctx, int NH, int NKV,
                                int P, int maxp) {
-    __shared__ float red[kThreads / 32];
-    __shared__ float lane_sum[8];
-    __shared__ float inv_sh;
-    __shared__ int zero_sh;
-    __shared__ __align__(16) float ebuf[kSumChunk];
-    __shared__ __align__(16) uint4 vbuf[2][kPvChunk * kD / 8];
-    __shared__ float pbuf[2][kPvChunk];
+    extern __shared__ __align__(16) unsigned char pv_smem[];
+    using L = PvSmem<KVM>;
+    uint4 *vbuf = reinterpret_cast<uint4 *>(pv_smem);                              // [stage][64 * 16]
+    float *pbuf = reinterpret_cast<float *>(pv_smem + L::kV);                     // [stage][KVM][64]
+    float *ebuf_all = reinterpret_cast<float *>(pv_smem + L::kV + L::kP);         // SE: [KVM][max_ctx]
+    __shared__ float red[KVM][kThreads / 32];
+    __shared__ float lane_sum[KVM][8];
+    __shared__ float inv_sh[KVM];
+    __shared__ int zero_sh[KVM];
     pdl_launch_dependents();
     pdl_wait();
-    const int h = blockIdx.x, i = blockIdx.y, d = threadIdx.x;
+    const int kvh = blockIdx.x, i = blockIdx.y;
+    const int hh = threadIdx.x / kThreads, d = threadIdx.x % kThreads;
+    const int h = kvh * KVM + hh;
     const int pos = positions[i];
     float *o = out + ((size_t)i * NH + h) * kD;
     if (pos < 0 || pos >= max_ctx) return;
     const int n = pos + 1, n8 = (n / 8) * 8;
     float *s = scores + ((size_t)i * NH + h) * max_ctx;
+    float *ebuf = ebuf_all + (size_t)hh * (SE ? max_ctx : kSumChunk);
+    float *e = SE ? ebuf : s;              // where the score row / exponentials live
+    if constexpr (SE) {
+        for (int t = d; t < n; t += kThreads) ebuf[t] = s[t];
+        __syncthreads();
+    }
     // 1. maximum (order-free)
     float m = -__int_as_float(0x7f800000);
-    for (int t = d; t < n; t += kThreads) m = fmaxf(m, s[t]);
+    for (int t = d; t < n; t += kThreads) m = fmaxf(m, e[t]);
 #pragma unroll
     for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if ((d & 31) == 0) red[d >> 5] = m;
+    if ((d & 31) == 0) red[hh][d >> 5] = m;
     __syncthreads();
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    if (!isfinite(m)) {          // every score -inf or NaN: the row is zeros
-        o[d] = 0.0f;
-        return;
-    }
+    m = fmaxf(fmaxf(red[hh][0], red[hh][1]), fmaxf(red[hh][2], red[hh][3]));
+    const bool finite_max = isfinite(m);   // every score -inf or NaN: the row is zeros
     // 2. exponentials in place (-inf scores give 0)
     const float ninf = -__int_as_float(0x7f800000);
-    for (int t = d; t < n; t += kThreads) {
-        const float x = s[t];
-        s[t] = x > ninf ? exp_ref(add_rn(x, -m)) : 0.0f;
-    }
+    if (finite_max)
+        for (int t = d; t < n; t += kThreads) {
+            const float x = e[t];
+            e[t] = x > ninf ? exp_ref(add_rn(x, -m)) : 0.0f;
+        }
     __syncthreads();
     // 3. the sum: 8 float lanes t-ascending, the lanes in double, the tail in double
     float acc8 = 0.0f;
-    for (int c0 = 0; c0 < n8; c0 += kSumChunk) {
-        const int cn = min(kSumChunk, n8 - c0);
-        for (int t = d; t < cn; t += kThreads) ebuf[t] = s[c0 + t];
-        __syncthreads();
+    if constexpr (SE) {
         if (d < 8)
-            for (int k = d; k < cn; k += 8) acc8 = add_rn(acc8, ebuf[k]);
-        __syncthreads();
+            for (int k = d; k < n8; k += 8) acc8 = add_rn(acc8, ebuf[k]);
+    } else {
+        for (int c0 = 0; c0 < n8; c0 += kSumChunk) {
+            const int cn = min(kSumChunk, n8 - c0);
+            for (int t = d; t < cn; t += kThreads) ebuf[t] = s[c0 + t];
+            __syncthreads();
+            if (d < 8)
+                for (int k = d; k < cn; k += 8) acc8 = add_rn(acc8, ebuf[k]);
+            __syncthreads();
+        }
     }
-    if (d < 8) lane_sum[d] = acc8;
+    if (d < 8) lane_sum[hh][d] = acc8;
     __syncthreads();
     if (d == 0) {
         double sum = 0.0;
-        for (int l = 0; l < 8; ++l) sum = __dadd_rn(sum, (double)lane_sum[l]);
-        for (int t = n8; t < n; ++t) sum = __dadd_rn(sum, (double)s[t]);
-        zero_sh = !(sum > 0.0) || !isfinite(sum);
-        inv_sh = __double2float_rn(__ddiv_rn(1.0, sum));
+        for (int l = 0; l < 8; ++l) sum = __dadd_rn(sum, (double)lane_sum[hh][l]);
+        for (int t = n8; t < n; ++t) sum = __dadd_rn(sum, (double)e[t]);
+        zero_sh[hh] = !finite_max || !(sum > 0.0) || !isfinite(sum);
+        inv_sh[hh] = __double2float_rn(__ddiv_rn(1.0, sum));
     }
     __syncthreads();
-    if (zero_sh) {
-        o[d] = 0.0f;
-        return;
+    const bool zero = zero_sh[hh] != 0;
+    const float inv = inv_sh[hh];
+    if constexpr (SE) {
+        // probabilities in place
+        for (int t = d; t < n; t += kThreads) ebuf[t] = zero ? 0.0f : mul_rn(ebuf[t], inv);
+        __syncthreads();
     }
-    const float inv = inv_sh;
-    // 4. P.V: one fma chain per d over t ascending, V staged by cp.async
+    // 4. P.V: one fma chain per (head, d) over t ascending; V staged once for
+    //    the KVM heads
     const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
-    const int kvh = h / (NH / NKV);
     const int nch = (n + kPvChunk - 1) / kPvChunk;
     auto issue = [&](int c) {
-        const int c0 = c * kPvChunk, cn = min(kPvChunk, n - c0);
-        uint4 *vb = vbuf[c & 1];
-        for (int e = d; e < cn * (kD / 8); e += kThreads) {
-            const int r = e / (kD / 8), q = e - r * (kD / 8);
-            cp_async16(vb + e, reinterpret_cast<const uint4 *>(v_pages + kv_index(pt_row, c0 + r, kvh, NKV, P)) + q);
+        if (c < nch) {
+            const int c0 = c * kPvChunk, cn = min(kPvChunk, n - c0);
+            const int st = c % kPvStages;
+            uint4 *vb = vbuf + st * (kPvChunk * kD / 8);
+            for (int x = threadIdx.x; x < cn * (kD / 8); x += KVM * kThreads) {
+                const int r = x / (kD / 8), q = x - r * (kD / 8);
+                cp_async16(vb + x,
+                           reinterpret_cast<const uint4 *>(v_pages + kv_index(pt_row, c0 + r, kvh, NKV, P)) + q);
+            }
+            if (!SE && d < cn) pbuf[(st * KVM + hh) * kPvChunk + d] = zero ? 0.0f : mul_rn(s[c0 + d], inv);
         }
-        if (d < cn) pbuf[c & 1][d] = mul_rn(s[c0 + d], inv);
-        cp_async_commit();
+        cp_async_commit();    // an empty group past the end keeps the wait counts uniform
     };
-    issue(0);
+#pragma unroll
+    for (int c = 0; c < kPvStages - 1; ++c) issue(c);
     float acc = 0.0f;
     for (int c = 0; c < nch; ++c) {
-        if (c + 1 < nch) {
-            issue(c + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        issue(c + kPvStages - 1);
+        cp_async_wait<kPvStages - 1>();
         __syncthreads();
+        const int st = c % kPvStages;
         const int cn = min(kPvChunk, n - c * kPvChunk);
-        const __half *vb = reinterpret_cast<const __half *>(vbuf[c & 1]) + d;
-        const float *pb = pbuf[c & 1];
+        const __half *vb = reinterpret_cast<const __half *>(vbuf + st * (kPvChunk * kD / 8)) + d;
+        const float *pb = SE ? ebuf + c * kPvChunk : pbuf + (st * KVM + hh) * kPvChunk;
         int k = 0;
         for (; k + 8 <= cn; k += 8) {
             float pv[8], vv[8];
@@ -211,9 +270,10 @@ attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t
             for (int j = 0; j < 8; ++j) acc = fma_rn(pv[j], vv[j], acc);
         }
         for (; k < cn; ++k) acc = fma_rn(pb[k], __half2float(vb[k * kD]), acc);
-        __syncthreads();
+        __syncthreads();   // stage st is refilled by the next iteration's issue
     }
-    o[d] = acc;
+    cp_async_wait<0>();
+    o[d] = zero ? 0.0f : acc;
 }
 
 size_t attn_ordered_workspace_bytes(size_t nq, int max_ctx, int NH) {
@@ -231,14 +291,40 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
     cfg.stream = stream;
     cfg.gridDim = dim3((a.max_ctx + kThreads - 1) / kThreads, a.NKV, (unsigned)a.nq);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)(a.NH / a.NKV) * kD * sizeof(float);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_ordered_scores_kernel, a.q, a.k_pages, a.page_table, a.seq_ids,
-                                       a.positions, scores, a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+    cfg.dynamicSmemBytes = (size_t)(a.NH / a.NKV) * kD * sizeof(float) + (size_t)kThreads * kKRow;
+    const int kvm = a.NH / a.NKV;
+    auto sc = [&](auto kern) {
+        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)cfg.dynamicSmemBytes);
+        if (e2 != cudaSuccess) return e2;
+        return cudaLaunchKernelEx(&cfg, kern, a.q, a.k_pages, a.page_table, a.seq_ids, a.positions, scores,
+                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+    };
+    cudaError_t e = kvm == 1 ? sc(attn_ordered_scores_kernel<1>)
+                  : kvm == 2 ? sc(attn_ordered_scores_kernel<2>)
+                  : kvm == 4 ? sc(attn_ordered_scores_kernel<4>) : cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3(a.NH, (unsigned)a.nq);
-    cfg.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&cfg, attn_ordered_softmax_pv_kernel, a.v_pages, a.page_table, a.seq_ids,
-                              a.positions, scores, a.out, a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+    cfg.gridDim = dim3(a.NKV, (unsigned)a.nq);
+    auto pv = [&](auto kern, size_t smem) {
+        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e2 != cudaSuccess) return e2;
+        cfg.blockDim = dim3(kvm * kThreads);
+        cfg.dynamicSmemBytes = smem;
+        return cudaLaunchKernelEx(&cfg, kern, a.v_pages, a.page_table, a.seq_ids, a.positions, scores, a.out,
+                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+    };
+    // the score rows in shared memory when they fit
+    const bool se = a.max_ctx <= kSmemCtx;
+    auto se_bytes = [&](int m) { return PvSmem<1>::kV + (size_t)kPvStages * m * kPvChunk * 4 + (size_t)m * a.max_ctx * 4; };
+    if (se) {
+        if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true>, se_bytes(1));
+        if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true>, se_bytes(2));
+        if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true>, se_bytes(4));
+    }
+    if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, false>, PvSmem<1>::kBytes);
+    if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, false>, PvSmem<2>::kBytes);
+    if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, false>, PvSmem<4>::kBytes);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace qvl
