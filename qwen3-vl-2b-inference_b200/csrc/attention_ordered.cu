@@ -66,10 +66,13 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
     unsigned char *ks = reinterpret_cast<unsigned char *>(qs + kvm * kD);
     const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
     const int rows = min(kThreads, pos + 1 - t0);
+    __shared__ size_t rowoff[kThreads];     // 16-byte index of each staged key row (one page lookup per row)
+    if (threadIdx.x < rows) rowoff[threadIdx.x] = kv_index(pt_row, t0 + threadIdx.x, kvh, NKV, P) / 8;
+    __syncthreads();
+    const uint4 *kp = reinterpret_cast<const uint4 *>(k_pages);
     for (int e = threadIdx.x; e < rows * 16; e += kThreads) {
         const int r = e >> 4, c = e & 15;
-        cp_async16(ks + r * kKRow + c * 16,
-                   reinterpret_cast<const uint4 *>(k_pages + kv_index(pt_row, t0 + r, kvh, NKV, P)) + c);
+        cp_async16(ks + r * kKRow + c * 16, kp + rowoff[r] + c);
     }
     cp_async_commit();
     for (int e = threadIdx.x; e < kvm * kD; e += blockDim.x) qs[e] = q[((size_t)i * NH + kvh * kvm) * kD + e];
@@ -100,13 +103,26 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
         }
 #pragma unroll
         for (int hh = 0; hh < KVM; ++hh) {
-            const float *qv = qs + hh * kD + 8 * c;
+            const float4 qa = reinterpret_cast<const float4 *>(qs + hh * kD + 8 * c)[0];
+            const float4 qb = reinterpret_cast<const float4 *>(qs + hh * kD + 8 * c)[1];
             if (!tail) {
-#pragma unroll
-                for (int l = 0; l < 8; ++l) l8[hh][l] = fma_rn(qv[l], kc[l], l8[hh][l]);
+                l8[hh][0] = fma_rn(qa.x, kc[0], l8[hh][0]);
+                l8[hh][1] = fma_rn(qa.y, kc[1], l8[hh][1]);
+                l8[hh][2] = fma_rn(qa.z, kc[2], l8[hh][2]);
+                l8[hh][3] = fma_rn(qa.w, kc[3], l8[hh][3]);
+                l8[hh][4] = fma_rn(qb.x, kc[4], l8[hh][4]);
+                l8[hh][5] = fma_rn(qb.y, kc[5], l8[hh][5]);
+                l8[hh][6] = fma_rn(qb.z, kc[6], l8[hh][6]);
+                l8[hh][7] = fma_rn(qb.w, kc[7], l8[hh][7]);
             } else {
-#pragma unroll
-                for (int l = 0; l < 8; ++l) l8[hh][l] = add_rn(l8[hh][l], mul_rn(qv[l], kc[l]));
+                l8[hh][0] = add_rn(l8[hh][0], mul_rn(qa.x, kc[0]));
+                l8[hh][1] = add_rn(l8[hh][1], mul_rn(qa.y, kc[1]));
+                l8[hh][2] = add_rn(l8[hh][2], mul_rn(qa.z, kc[2]));
+                l8[hh][3] = add_rn(l8[hh][3], mul_rn(qa.w, kc[3]));
+                l8[hh][4] = add_rn(l8[hh][4], mul_rn(qb.x, kc[4]));
+                l8[hh][5] = add_rn(l8[hh][5], mul_rn(qb.y, kc[5]));
+                l8[hh][6] = add_rn(l8[hh][6], mul_rn(qb.z, kc[6]));
+                l8[hh][7] = add_rn(l8[hh][7], mul_rn(qb.w, kc[7]));
             }
         }
     }
@@ -114,7 +130,10 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
     for (int hh = 0; hh < KVM; ++hh) {
         float r;
         if (!tail) {
-            r = reduce8_ref(l8[hh]);
+            // reduce8_ref's order: (v0+v4, v1+v5, v2+v6, v3+v7), then (u0+u1)+(u2+u3)
+            const float u0 = add_rn(l8[hh][0], l8[hh][4]), u1 = add_rn(l8[hh][1], l8[hh][5]);
+            const float u2 = add_rn(l8[hh][2], l8[hh][6]), u3 = add_rn(l8[hh][3], l8[hh][7]);
+            r = add_rn(add_rn(u0, u1), add_rn(u2, u3));
         } else {
             r = l8[hh][0];
 #pragma unroll
@@ -174,8 +193,49 @@ attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t
     if (pos < 0 || pos >= max_ctx) return;
     const int n = pos + 1, n8 = (n / 8) * 8;
     float *s = scores + ((size_t)i * NH + h) * max_ctx;
-    float *ebuf = ebuf_all + (size_t)hh * (SE ? max_ctx : kSumChunk);
+    float *ebuf = ebuf_all + (size_t)hh * (SE ? ((max_ctx + 3) & ~3) : kSumChunk);   // rows 16-byte aligned
     float *e = SE ? ebuf : s;              // where the score row / exponentials live
+    // V rows do not depend on the softmax: the first stages of the P.V ring
+    // are in flight from here on
+    const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
+    const int nch = (n + kPvChunk - 1) / kPvChunk;
+    // thread x of the block copies 16-byte column x & 15 of rows
+    // (x >> 4) + j * kRowStep of every chunk; their pages and slots advance
+    // by 64 positions per chunk (no division after the first)
+    constexpr int kRowStep = KVM * kThreads / 16, kRowsPer = kPvChunk / kRowStep;
+    const int qcol = threadIdx.x & 15;
+    int pg[kRowsPer], slot[kRowsPer];
+#pragma unroll
+    for (int j = 0; j < kRowsPer; ++j) {
+        const int t = (threadIdx.x >> 4) + j * kRowStep;
+        pg[j] = t / P;
+        slot[j] = t - pg[j] * P;
+    }
+    const uint4 *vp = reinterpret_cast<const uint4 *>(v_pages);
+    auto issue = [&](int c) {
+        if (c < nch) {
+            const int cn = min(kPvChunk, n - c * kPvChunk);
+            uint4 *vb = vbuf + (c % kPvStages) * (kPvChunk * kD / 8);
+#pragma unroll
+            for (int j = 0; j < kRowsPer; ++j) {
+                const int r = (threadIdx.x >> 4) + j * kRowStep;
+                if (r < cn)
+                    cp_async16(vb + r * 16 + qcol,
+                               vp + (((size_t)pt_row[pg[j]] * NKV + kvh) * P + slot[j]) * (kD / 8) + qcol);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kRowsPer; ++j) {
+            slot[j] += kPvChunk;
+            while (slot[j] >= P) {
+                slot[j] -= P;
+                ++pg[j];
+            }
+        }
+        cp_async_commit();    // an empty group past the end keeps the wait counts uniform
+    };
+#pragma unroll
+    for (int c = 0; c < kPvStages - 1; ++c) issue(c);
     if constexpr (SE) {
         for (int t = d; t < n; t += kThreads) ebuf[t] = s[t];
         __syncthreads();
@@ -231,43 +291,31 @@ attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t
     }
     // 4. P.V: one fma chain per (head, d) over t ascending; V staged once for
     //    the KVM heads
-    const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
-    const int nch = (n + kPvChunk - 1) / kPvChunk;
-    auto issue = [&](int c) {
-        if (c < nch) {
-            const int c0 = c * kPvChunk, cn = min(kPvChunk, n - c0);
-            const int st = c % kPvStages;
-            uint4 *vb = vbuf + st * (kPvChunk * kD / 8);
-            for (int x = threadIdx.x; x < cn * (kD / 8); x += KVM * kThreads) {
-                const int r = x / (kD / 8), q = x - r * (kD / 8);
-                cp_async16(vb + x,
-                           reinterpret_cast<const uint4 *>(v_pages + kv_index(pt_row, c0 + r, kvh, NKV, P)) + q);
-            }
-            if (!SE && d < cn) pbuf[(st * KVM + hh) * kPvChunk + d] = zero ? 0.0f : mul_rn(s[c0 + d], inv);
-        }
-        cp_async_commit();    // an empty group past the end keeps the wait counts uniform
-    };
-#pragma unroll
-    for (int c = 0; c < kPvStages - 1; ++c) issue(c);
     float acc = 0.0f;
     for (int c = 0; c < nch; ++c) {
         issue(c + kPvStages - 1);
-        cp_async_wait<kPvStages - 1>();
-        __syncthreads();
         const int st = c % kPvStages;
         const int cn = min(kPvChunk, n - c * kPvChunk);
+        if (!SE && d < cn) pbuf[(st * KVM + hh) * kPvChunk + d] = zero ? 0.0f : mul_rn(s[c * kPvChunk + d], inv);
+        cp_async_wait<kPvStages - 1>();
+        __syncthreads();
         const __half *vb = reinterpret_cast<const __half *>(vbuf + st * (kPvChunk * kD / 8)) + d;
         const float *pb = SE ? ebuf + c * kPvChunk : pbuf + (st * KVM + hh) * kPvChunk;
         int k = 0;
         for (; k + 8 <= cn; k += 8) {
-            float pv[8], vv[8];
+            const float4 pa = reinterpret_cast<const float4 *>(pb + k)[0];
+            const float4 pc = reinterpret_cast<const float4 *>(pb + k)[1];
+            float vv[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                pv[j] = pb[k + j];
-                vv[j] = __half2float(vb[(k + j) * kD]);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc = fma_rn(pv[j], vv[j], acc);
+            for (int j = 0; j < 8; ++j) vv[j] = __half2float(vb[(k + j) * kD]);
+            acc = fma_rn(pa.x, vv[0], acc);
+            acc = fma_rn(pa.y, vv[1], acc);
+            acc = fma_rn(pa.z, vv[2], acc);
+            acc = fma_rn(pa.w, vv[3], acc);
+            acc = fma_rn(pc.x, vv[4], acc);
+            acc = fma_rn(pc.y, vv[5], acc);
+            acc = fma_rn(pc.z, vv[6], acc);
+            acc = fma_rn(pc.w, vv[7], acc);
         }
         for (; k < cn; ++k) acc = fma_rn(pb[k], __half2float(vb[k * kD]), acc);
         __syncthreads();   // stage st is refilled by the next iteration's issue
@@ -315,7 +363,7 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
     };
     // the score rows in shared memory when they fit
     const bool se = a.max_ctx <= kSmemCtx;
-    auto se_bytes = [&](int m) { return PvSmem<1>::kV + (size_t)kPvStages * m * kPvChunk * 4 + (size_t)m * a.max_ctx * 4; };
+    auto se_bytes = [&](int m) { return PvSmem<1>::kV + (size_t)kPvStages * m * kPvChunk * 4 + (size_t)m * ((a.max_ctx + 3) & ~3) * 4; };
     if (se) {
         if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true>, se_bytes(1));
         if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true>, se_bytes(2));
