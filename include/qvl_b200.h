@@ -85,6 +85,10 @@ const char *qvl_version(void);
  * 8-byte aligned. */
 int qvl_quantize_rows(const float *x, int16_t *q, float *q_scales,
                       size_t M, size_t K, size_t group_size, void *stream);
+/* qvl_quantize_rows that also writes the hi/lo planes of q (see
+ * qvl_linear_planes_i8_batched); hi/lo 4-byte aligned. */
+int qvl_quantize_rows_planes(const float *x, int16_t *q, float *q_scales, int8_t *hi, uint8_t *lo, size_t M,
+                             size_t K, size_t group_size, void *stream);
 
 /* ---- INT8 linear: C[M,N] = A[M,K] . dequant(B[N,K])^T, fp32 in/out -------
  * Replaces linear()'s INT8 branch (matmul/src/cpu_wrapper.cpp:339-357) and
@@ -164,6 +168,14 @@ int qvl_linear_q16_i8_batched(const int16_t *q, const float *q_scales, size_t n_
                               const int8_t *const *B, const float *const *B_scales, float *const *C,
                               const size_t *N, size_t M, size_t K, int semantics, int swiglu_pair,
                               float *up_scratch, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The same products from activations already split into the tensor cores'
+ * hi/lo planes (hi = q >> 8 int8, lo = q & 255 uint8, [M, K] each, 16-byte
+ * aligned) -- as the *_planes producers below write them -- in one launch
+ * over all n_mats (<= 3) matrices.  TILED order, per-output-row scales. */
+int qvl_linear_planes_i8_batched(const int8_t *hi, const uint8_t *lo, const float *q_scales, size_t n_mats,
+                                 const int8_t *const *B, const float *const *B_scales, float *const *C,
+                                 const size_t *N, size_t M, size_t K, int semantics, void *stream);
 
 /* ---- SwiGLU (layers/src/text_layer.cpp:420-434) ------------------------
  * gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i], in place, n elements. */
@@ -285,6 +297,11 @@ int qvl_qknorm_rope_kv_append(float *q, const float *k_new, const float *v_new, 
 int qvl_rms_norm_i8(const float *x, const int8_t *w, const float *w_scales, float *out,
                     int16_t *q, float *q_scales, size_t rows, size_t hidden, size_t norm_group,
                     float eps, int inplace_form, size_t quant_group, void *stream);
+/* qvl_rms_norm_i8 with per-row quantisation (group = hidden) that also
+ * writes the hi/lo planes of q for qvl_linear_planes_i8_batched. */
+int qvl_rms_norm_i8_planes(const float *x, const int8_t *w, const float *w_scales, float *out, int16_t *q,
+                           float *q_scales, int8_t *hi, uint8_t *lo, size_t rows, size_t hidden,
+                           size_t norm_group, float eps, int inplace_form, void *stream);
 /* embedding_lookup for an INT8 table with per-row scales (the tied
  * embedding / LM-head matrix): out[t] = table[ids[t]] * row_scales[ids[t]]. */
 int qvl_embedding_lookup_i8(const int8_t *table, const float *row_scales, const int32_t *token_ids,

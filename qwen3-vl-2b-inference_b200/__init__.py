@@ -50,7 +50,7 @@ EXPORTED = (
     "qvl_text_decode_step_ex",
     "qvl_text_decode_abort_flag", "qvl_text_decode_trace", "qvl_tc_timeout_status",
     "qvl_attention_decode_static", "qvl_attention_ordered_workspace_bytes", "qvl_attention_decode_ordered",
-    "qvl_rope_table",
+    "qvl_rope_table", "qvl_quantize_rows_planes", "qvl_rms_norm_i8_planes", "qvl_linear_planes_i8_batched",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -139,6 +139,9 @@ def load_library(path: str = LIB_PATH):
     L.qvl_text_decode_trace.argtypes = [_P]
     L.qvl_tc_timeout_status.argtypes = [ctypes.POINTER(_I), _I, _P]
     L.qvl_rope_table.argtypes = [_I, _I, _I, _P, _P]
+    L.qvl_quantize_rows_planes.argtypes = [_P] * 5 + [_Z, _Z, _Z, _P]
+    L.qvl_rms_norm_i8_planes.argtypes = [_P] * 8 + [_Z, _Z, _Z, ctypes.c_float, _I, _P]
+    L.qvl_linear_planes_i8_batched.argtypes = [_P, _P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _I, _P]
     L.qvl_internal_set_tc_timeout.argtypes = [_P]
     _lib = L
     return L
@@ -488,6 +491,48 @@ def linear_batched(q, q_scales, mats, outs, workspace, semantics=SEM_TILED, swig
     _check(L.qvl_linear_q16_i8_batched(_ptr(q), _ptr(q_scales), n, Bp, Sp, Cp, Np, M, K, semantics,
                                        int(swiglu_pair), _ptr(up_scratch), _ptr(ws), ws.numel(), _stream(stream)),
            "linear_batched")
+    return outs
+
+
+class Planes:
+    """The tensor cores' hi/lo activation planes (hi = q >> 8, lo = q & 255)
+    of up to `rows` x `cols` quantised activations, reused across products."""
+
+    def __init__(self, rows, cols, device):
+        self.hi = torch.empty(rows * cols, dtype=torch.int8, device=device)
+        self.lo = torch.empty(rows * cols, dtype=torch.uint8, device=device)
+
+
+def quantize_rows_planes(x, q, q_scales, planes: Planes, group_size=0, stream=None):
+    """quantize_rows into q/q_scales that also fills `planes` for linear_planes_batched."""
+    M, K = x.shape
+    _check(load_library().qvl_quantize_rows_planes(_ptr(x), _ptr(q), _ptr(q_scales), _ptr(planes.hi),
+                                                   _ptr(planes.lo), M, K, group_size or K, _stream(stream)),
+           "quantize_rows_planes")
+    return q
+
+
+def rms_norm_i8_planes(x, w, w_scales, norm_group, eps, q, q_scales, planes: Planes, out=None, inplace_form=False,
+                       stream=None):
+    """rms_norm_i8 with per-row quantisation that also fills `planes`."""
+    rows, H = x.shape
+    _check(load_library().qvl_rms_norm_i8_planes(_ptr(x), _ptr(w), _ptr(w_scales), _ptr(out), _ptr(q),
+                                                 _ptr(q_scales), _ptr(planes.hi), _ptr(planes.lo), rows, H,
+                                                 norm_group, eps, int(inplace_form), _stream(stream)),
+           "rms_norm_i8_planes")
+    return out
+
+
+def linear_planes_batched(planes: Planes, q_scales, mats, outs, M, K, semantics=SEM_TILED, stream=None):
+    """Tensor-core products of activations already in `planes`, one launch for all (<= 3) matrices."""
+    n = len(mats)
+    Bp = (ctypes.c_void_p * n)(*[_ptr(w) for w, _ in mats])
+    Sp = (ctypes.c_void_p * n)(*[_ptr(s) for _, s in mats])
+    Cp = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    Np = (ctypes.c_size_t * n)(*[w.shape[0] for w, _ in mats])
+    _check(load_library().qvl_linear_planes_i8_batched(_ptr(planes.hi), _ptr(planes.lo), _ptr(q_scales), n, Bp, Sp,
+                                                       Cp, Np, M, K, semantics, _stream(stream)),
+           "linear_planes_batched")
     return outs
 
 

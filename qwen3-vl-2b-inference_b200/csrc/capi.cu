@@ -87,6 +87,24 @@ int run_q16_linear(const int16_t *q, const float *qs, const int8_t *B, const flo
     return QVL_OK;
 }
 
+// The products of one set of hi/lo planes: a single tensor-core launch over
+// all matrices; with up_scratch, matrix 1's product goes there and is folded
+// into matrix 0's as swiglu(C0, up) (gate/up pair).
+int run_planes_batched(const int8_t *hi, const uint8_t *lo, const float *q_scales, size_t n_mats,
+                       const int8_t *const *B, const float *const *B_scales, float *const *C, const size_t *N,
+                       size_t M, size_t K, int acc, float *up_scratch, cudaStream_t st) {
+    float *outs[3];
+    int Ns[3];
+    for (size_t i = 0; i < n_mats; ++i) {
+        outs[i] = (up_scratch && i == 1) ? up_scratch : C[i];
+        Ns[i] = (int)N[i];
+    }
+    QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes_multi(hi, lo, q_scales, (int)n_mats, B, B_scales, outs, Ns, (int)M,
+                                                     (int)K, acc, st));
+    if (up_scratch) QVL_CUDA_TRY(qvl::launch_swiglu(C[0], up_scratch, (long)(M * N[0]), st));
+    return QVL_OK;
+}
+
 int check_linear_shape(size_t M, size_t N, size_t K, size_t g) {
     if (M == 0 || N == 0 || K == 0) return QVL_ERR_INVALID;
     if (K > (1u << 30) || N > (1u << 30) || M > (1u << 20)) return QVL_ERR_INVALID;
@@ -395,13 +413,24 @@ int qvl_linear_q16_i8_batched(const int16_t *q, const float *q_scales, size_t n_
     int8_t *hi = static_cast<int8_t *>(workspace);
     uint8_t *lo = reinterpret_cast<uint8_t *>(hi) + need / 2;
     QVL_CUDA_TRY(qvl::launch_split_hi_lo(q, hi, lo, (int)M, (int)K, st));
+    return run_planes_batched(hi, lo, q_scales, n_mats, B, B_scales, C, N, M, K, acc, swiglu_pair ? up_scratch : nullptr,
+                              st);
+}
+
+int qvl_linear_planes_i8_batched(const int8_t *hi, const uint8_t *lo, const float *q_scales, size_t n_mats,
+                                 const int8_t *const *B, const float *const *B_scales, float *const *C,
+                                 const size_t *N, size_t M, size_t K, int semantics, void *stream) {
+    if (!hi || !lo || !q_scales || !B || !B_scales || !C || !N || n_mats == 0 || n_mats > 3) return QVL_ERR_INVALID;
+    const int acc = (semantics & QVL_SEM_ACCUMULATE) ? 1 : 0;
+    const int sem = semantics & ~QVL_SEM_ACCUMULATE;
+    if (sem != QVL_SEM_TILED && !(sem == QVL_SEM_REFERENCE && M > 1)) return QVL_ERR_UNSUPPORTED;
+    if (!aligned(hi, 16) || !aligned(lo, 16) || (M * K) % 16) return QVL_ERR_INVALID;
     for (size_t i = 0; i < n_mats; ++i) {
-        float *out = (swiglu_pair && i == 1) ? up_scratch : C[i];
-        QVL_CUDA_TRY(qvl::launch_gemm_i8_tc_planes(hi, lo, q_scales, B[i], B_scales[i], out, (int)M, (int)N[i],
-                                                   (int)K, acc, st));
+        if (!B[i] || !B_scales[i] || !C[i] || !aligned(B[i], 16)) return QVL_ERR_INVALID;
+        if (!qvl::gemm_tc_supported(M, N[i], K, K)) return QVL_ERR_UNSUPPORTED;
     }
-    if (swiglu_pair) QVL_CUDA_TRY(qvl::launch_swiglu(C[0], up_scratch, (long)(M * N[0]), st));
-    return QVL_OK;
+    return run_planes_batched(hi, lo, q_scales, n_mats, B, B_scales, C, N, M, K, acc, nullptr,
+                              (cudaStream_t)stream);
 }
 
 // Test hook: the expf the SwiGLU kernels use, elementwise (not in the header).
@@ -555,6 +584,30 @@ int qvl_rms_norm_i8(const float *x, const int8_t *w, const float *w_scales, floa
     QVL_CUDA_TRY(qvl::launch_rmsnorm_quant(x, w, w_scales, out, q, q_scales, (int)rows, (int)hidden,
                                            (int)norm_group, eps, inplace_form != 0,
                                            q ? (int)quant_group : 16, (cudaStream_t)stream));
+    return QVL_OK;
+}
+
+int qvl_rms_norm_i8_planes(const float *x, const int8_t *w, const float *w_scales, float *out, int16_t *q,
+                           float *q_scales, int8_t *hi, uint8_t *lo, size_t rows, size_t hidden,
+                           size_t norm_group, float eps, int inplace_form, void *stream) {
+    if (!x || !w || !w_scales || !q || !q_scales || !hi || !lo) return QVL_ERR_INVALID;
+    if (rows == 0) return QVL_OK;
+    if (hidden == 0 || hidden % 16 || hidden > 16384 || norm_group == 0 || hidden % norm_group)
+        return QVL_ERR_INVALID;
+    if (!aligned(x, 16) || !aligned(q, 8) || !aligned(hi, 4) || !aligned(lo, 4)) return QVL_ERR_INVALID;
+    QVL_CUDA_TRY(qvl::launch_rmsnorm_quant(x, w, w_scales, out, q, q_scales, (int)rows, (int)hidden,
+                                           (int)norm_group, eps, inplace_form != 0, (int)hidden,
+                                           (cudaStream_t)stream, hi, lo));
+    return QVL_OK;
+}
+
+int qvl_quantize_rows_planes(const float *x, int16_t *q, float *q_scales, int8_t *hi, uint8_t *lo, size_t M,
+                             size_t K, size_t group_size, void *stream) {
+    if (!x || !q || !q_scales || !hi || !lo) return QVL_ERR_INVALID;
+    if (!aligned(x, 16) || !aligned(q, 8) || !aligned(hi, 4) || !aligned(lo, 4)) return QVL_ERR_INVALID;
+    if (M == 0 || K == 0 || group_size == 0 || K % group_size || group_size % 16) return QVL_ERR_INVALID;
+    QVL_CUDA_TRY(qvl::launch_quantize_rows(x, q, q_scales, (int)M, (int)K, (int)group_size,
+                                           (cudaStream_t)stream, hi, lo));
     return QVL_OK;
 }
 

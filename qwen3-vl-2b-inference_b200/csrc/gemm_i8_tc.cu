@@ -99,15 +99,32 @@ __device__ __forceinline__ void epilogue_rows(uint32_t d_hi, uint32_t d_lo, uint
     }
 }
 
-// grid: (ceil(M/NT), ceil(N/128), SPLIT); block 128; with SPLIT > 1 the SPLIT
-// CTAs of a cluster (1, 1, SPLIT) each take K/SPLIT and their exact int32
-// partial sums are added through distributed shared memory (split-K keeps
-// small-N products -- decode batches -- spread over the GPU).
+// Up to three weight matrices of the same activations in one launch (q/k/v,
+// gate/up): their 128-row weight tiles are numbered one after the other.
+constexpr int kMaxMats = 3;
+struct TcMats {
+    CUtensorMap w[kMaxMats];
+    const float *ws[kMaxMats];
+    float *C[kMaxMats];
+    int N[kMaxMats];
+    int tile0[kMaxMats + 1];   // first weight tile of each matrix; tile0[n] = all tiles
+    int n;
+};
+
+// grid: (ceil(M/NT), weight tiles of all matrices, SPLIT); block 128; with
+// SPLIT > 1 the SPLIT CTAs of a cluster (1, 1, SPLIT) each take K/SPLIT and
+// their exact int32 partial sums are added through distributed shared memory
+// (split-K keeps small-N products -- decode batches -- spread over the GPU).
 template <int NT, int SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hi,
-                  const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale,
-                  const float *__restrict w_scale, float *__restrict C, int M, int N, int K, int acc) {
+gemm_i8_tc_kernel(const __grid_constant__ TcMats mats, const __grid_constant__ CUtensorMap tm_hi,
+                  const __grid_constant__ CUtensorMap tm_lo, const float *__restrict a_scale, int M, int K,
+                  int acc) {
+    const int mi = (mats.n > 1 && (int)blockIdx.y >= mats.tile0[1]) + (mats.n > 2 && (int)blockIdx.y >= mats.tile0[2]);
+    const CUtensorMap *tm_w = &mats.w[mi];
+    const float *__restrict w_scale = mats.ws[mi];
+    float *__restrict C = mats.C[mi];
+    const int N = mats.N[mi];
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -122,7 +139,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // x = activation tile (fastest): the CTAs that share a weight tile run
     // together, so the tile is read from HBM once and from L2 after
-    const int n0 = blockIdx.y * kBM;
+    const int n0 = ((int)blockIdx.y - mats.tile0[mi]) * kBM;
     const int m0 = blockIdx.x * NT;
     const int nk = K / kBK / SPLIT;             // stages of this CTA's K slice
     const int kb0 = blockIdx.z * nk;
@@ -135,7 +152,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
         }
         tc::mbar_init(accbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        tc::prefetch_tmap(&tm_w);
+        tc::prefetch_tmap(tm_w);
         tc::prefetch_tmap(&tm_hi);
         tc::prefetch_tmap(&tm_lo);
     }
@@ -170,7 +187,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
             if (!ok) break;
             unsigned char *st = smem + s * L::kStage;
             tc::mbar_expect_tx(full0 + 8 * s, L::kStage);
-            tc::tma_load_2d(tc::smem_u32(st), &tm_w, (kb0 + kb) * kBK, n0, full0 + 8 * s);
+            tc::tma_load_2d(tc::smem_u32(st), tm_w, (kb0 + kb) * kBK, n0, full0 + 8 * s);
             if (kb == 0) pdl_wait();   // activations come from the previous kernel
             tc::tma_load_2d(tc::smem_u32(st + L::kA), &tm_hi, (kb0 + kb) * kBK, m0, full0 + 8 * s);
             tc::tma_load_2d(tc::smem_u32(st + L::kA + L::kB), &tm_lo, (kb0 + kb) * kBK, m0, full0 + 8 * s);
@@ -685,14 +702,14 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
 }
 
 template <int NT, int SPLIT>
-cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml, const float *as,
-                      const float *ws, float *C, int M, int N, int K, int acc, cudaStream_t st) {
+cudaError_t launch_nt(const TcMats &mats, const CUtensorMap &mh, const CUtensorMap &ml, const float *as, int M,
+                      int K, int acc, cudaStream_t st) {
     auto kern = gemm_i8_tc_kernel<NT, SPLIT>;
     const int smem = TcSmem<NT>::kBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((M + NT - 1) / NT, (N + kBM - 1) / kBM, SPLIT);
+    cfg.gridDim = dim3((M + NT - 1) / NT, mats.tile0[mats.n], SPLIT);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -705,18 +722,17 @@ cudaError_t launch_nt(const CUtensorMap &mw, const CUtensorMap &mh, const CUtens
     attr[1].val.clusterDim.z = SPLIT;
     cfg.attrs = attr;
     cfg.numAttrs = SPLIT > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, mw, mh, ml, as, ws, C, M, N, K, acc);
+    return cudaLaunchKernelEx(&cfg, kern, mats, mh, ml, as, M, K, acc);
 }
 
 template <int NT>
-cudaError_t launch_split(int split, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
-                         const float *as, const float *ws, float *C, int M, int N, int K, int acc,
-                         cudaStream_t st) {
+cudaError_t launch_split(int split, const TcMats &mats, const CUtensorMap &mh, const CUtensorMap &ml,
+                         const float *as, int M, int K, int acc, cudaStream_t st) {
     switch (split) {
-        case 8: return launch_nt<NT, 8>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
-        case 4: return launch_nt<NT, 4>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
-        case 2: return launch_nt<NT, 2>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
-        default: return launch_nt<NT, 1>(mw, mh, ml, as, ws, C, M, N, K, acc, st);
+        case 8: return launch_nt<NT, 8>(mats, mh, ml, as, M, K, acc, st);
+        case 4: return launch_nt<NT, 4>(mats, mh, ml, as, M, K, acc, st);
+        case 2: return launch_nt<NT, 2>(mats, mh, ml, as, M, K, acc, st);
+        default: return launch_nt<NT, 1>(mats, mh, ml, as, M, K, acc, st);
     }
 }
 
@@ -833,23 +849,44 @@ cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const 
         }
         return launch_grouped<32, 4>(mw, mh, ml, qs, ws, C, M, N, K, g, acc, stream);
     }
-    // Activation tile: 128 rows from M >= 256 (64 from 64, else 32).  Products
-    // of two or more waves of 128 x 128 tiles run on the persistent kernel;
-    // smaller ones split K over a cluster until there are ~2 CTAs per SM
-    // (exact int32 partial sums, added through distributed shared memory).
+    const int8_t *Ws[1] = {W};
+    const float *wss[1] = {ws};
+    float *Cs[1] = {C};
+    const int Ns[1] = {N};
+    return launch_gemm_i8_tc_planes_multi(hi, lo, qs, 1, Ws, wss, Cs, Ns, M, K, acc, stream);
+}
+
+cudaError_t launch_gemm_i8_tc_planes_multi(const int8_t *hi, const uint8_t *lo, const float *qs, int n_mats,
+                                           const int8_t *const *W, const float *const *ws, float *const *C,
+                                           const int *N, int M, int K, int acc, cudaStream_t stream) {
+    if (n_mats < 1 || n_mats > kMaxMats) return cudaErrorInvalidValue;
+    // Activation tile: 128 rows from M >= 256 (64 from 64, else 32).  A
+    // single product of two or more waves of 128 x 128 tiles runs on the
+    // persistent kernel; the others (and every multi-matrix launch) split K
+    // over a cluster until there are ~2 CTAs per SM (exact int32 partial
+    // sums, added through distributed shared memory).
     const int NT = M >= 256 ? 128 : (M >= 64 ? 64 : 32);
-    CUtensorMap mw, mh, ml;
-    if (!make_map(&mw, W, N, K, kBM) || !make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT))
-        return cudaErrorInvalidValue;
-    const long tiles = (long)((N + kBM - 1) / kBM) * ((M + NT - 1) / NT);
-    if (NT == 128 && tiles >= 2 * 148 && persist_enabled())
-        return launch_persistent<128>(mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    CUtensorMap mh, ml;
+    if (!make_map(&mh, hi, M, K, NT) || !make_map(&ml, lo, M, K, NT)) return cudaErrorInvalidValue;
+    TcMats mats = {};
+    mats.n = n_mats;
+    mats.tile0[0] = 0;
+    for (int i = 0; i < n_mats; ++i) {
+        if (!make_map(&mats.w[i], W[i], N[i], K, kBM)) return cudaErrorInvalidValue;
+        mats.ws[i] = ws[i];
+        mats.C[i] = C[i];
+        mats.N[i] = N[i];
+        mats.tile0[i + 1] = mats.tile0[i] + (N[i] + kBM - 1) / kBM;
+    }
+    const long tiles = (long)mats.tile0[n_mats] * ((M + NT - 1) / NT);
+    if (n_mats == 1 && NT == 128 && tiles >= 2 * 148 && persist_enabled())
+        return launch_persistent<128>(mats.w[0], mh, ml, qs, ws[0], C[0], M, N[0], K, acc, stream);
     const int nkb = K / kBK;
     int split = 1;
     while (split < 8 && tiles * split * 2 <= 2 * 148 && nkb % (split * 2) == 0) split *= 2;
-    if (NT == 128) return launch_split<128>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    if (NT == 64) return launch_split<64>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
-    return launch_split<32>(split, mw, mh, ml, qs, ws, C, M, N, K, acc, stream);
+    if (NT == 128) return launch_split<128>(split, mats, mh, ml, qs, M, K, acc, stream);
+    if (NT == 64) return launch_split<64>(split, mats, mh, ml, qs, M, K, acc, stream);
+    return launch_split<32>(split, mats, mh, ml, qs, M, K, acc, stream);
 }
 
 cudaError_t launch_gemm_i8_tc(const int16_t *q, const float *qs, int8_t *hi, uint8_t *lo, const int8_t *W,

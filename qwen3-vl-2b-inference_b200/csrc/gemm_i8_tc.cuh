@@ -22,4 +22,9 @@ cudaError_t launch_split_hi_lo(const int16_t *q, int8_t *hi, uint8_t *lo, int M,
 cudaError_t launch_gemm_i8_tc_planes(const int8_t *hi, const uint8_t *lo, const float *qs, const int8_t *W,
                                      const float *ws, float *C, int M, int N, int K, int acc,
                                      cudaStream_t stream, int g = 0);   // g: group size, 0 = K
+// One launch over up to three weight matrices [N_i, K] of the same hi/lo
+// activation planes (per-output-row scales): C_i = product_i (C_i += with acc).
+cudaError_t launch_gemm_i8_tc_planes_multi(const int8_t *hi, const uint8_t *lo, const float *qs, int n_mats,
+                                           const int8_t *const *W, const float *const *ws, float *const *C,
+                                           const int *N, int M, int K, int acc, cudaStream_t stream);
 }  // namespace qvl

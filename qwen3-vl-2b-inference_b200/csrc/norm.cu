@@ -21,7 +21,8 @@ namespace qvl {
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const float *x, const int8_t *__restrict wq,
                      const float *__restrict ws, float *out, int16_t *__restrict q,
-                     float *__restrict qs, int H, int ngs, float eps, int inplace_form, int qg) {
+                     float *__restrict qs, int H, int ngs, float eps, int inplace_form, int qg,
+                     int8_t *__restrict hi, uint8_t *__restrict lo) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float scratch[65];
     pdl_launch_dependents();
@@ -30,7 +31,8 @@ rmsnorm_quant_kernel(const float *x, const int8_t *__restrict wq,
     const int G = q ? H / qg : 0;
     cta_norm_quant_row(x + (size_t)row * H, wq, ws, ngs, eps, inplace_form != 0,
                        out ? out + (size_t)row * H : nullptr, q ? q + (size_t)row * H : nullptr,
-                       q ? qs + (size_t)row * G : nullptr, qg, H, sm, sm + H, scratch);
+                       q ? qs + (size_t)row * G : nullptr, qg, H, sm, sm + H, scratch,
+                       hi ? hi + (size_t)row * H : nullptr, lo ? lo + (size_t)row * H : nullptr);
 }
 
 // grid: n_tokens; block 256.  out[t] = (float)table[id] * scale[id]
@@ -58,7 +60,7 @@ static void pdl_attr(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStr
 
 cudaError_t launch_rmsnorm_quant(const float *x, const int8_t *wq, const float *ws, float *out,
                                  int16_t *q, float *qs, int rows, int H, int ngs, float eps,
-                                 bool inplace_form, int qg, cudaStream_t st) {
+                                 bool inplace_form, int qg, cudaStream_t st, int8_t *hi, uint8_t *lo) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     pdl_attr(cfg, attr, st);
@@ -71,7 +73,7 @@ cudaError_t launch_rmsnorm_quant(const float *x, const int8_t *wq, const float *
         if (e != cudaSuccess) return e;
     }
     return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, wq, ws, out, q, qs, H, ngs, eps,
-                              inplace_form ? 1 : 0, qg);
+                              inplace_form ? 1 : 0, qg, hi, lo);
 }
 
 cudaError_t launch_embedding_i8(const int8_t *table, const float *scales, const int32_t *ids, float *out,

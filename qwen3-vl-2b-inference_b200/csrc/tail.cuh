@@ -41,10 +41,12 @@ __device__ __forceinline__ float rms_inv(float ss, int H, float eps, bool inplac
     return inplace_form ? __fdiv_rn(1.0f, r) : __double2float_rn(1.0 / (double)r);
 }
 
-// Group scales of ts[0..H) (group g, G = H/g <= 64) and quantisation into q.
+// Group scales of ts[0..H) (group g, G = H/g <= 64) and quantisation into q
+// (and, when hi is given, the tensor-core planes hi = q >> 8, lo = q & 255).
 // scratch: >= 64 floats of shared memory.
 __device__ __forceinline__ void cta_quantize_smem_row(const float *ts, int H, int g, int16_t *q, float *qs,
-                                                      float *scratch) {
+                                                      float *scratch, int8_t *hi = nullptr,
+                                                      uint8_t *lo = nullptr) {
     const int G = H / g;
     const int hw = threadIdx.x >> 4, nhw = blockDim.x >> 4, t16 = threadIdx.x & 15;
     // both half-warps of a warp take the same trip count (full-mask shuffles)
@@ -59,7 +61,19 @@ __device__ __forceinline__ void cta_quantize_smem_row(const float *ts, int H, in
         }
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < H; j += blockDim.x) q[j] = quant_one(ts[j], scratch[j / g]);
+    if (hi) {
+        for (int j4 = threadIdx.x; j4 < H / 4; j4 += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4 *>(ts)[j4];
+            const float inv = scratch[(4 * j4) / g];
+            const uint32_t a = (uint16_t)quant_one(v.x, inv), b = (uint16_t)quant_one(v.y, inv);
+            const uint32_t c = (uint16_t)quant_one(v.z, inv), d = (uint16_t)quant_one(v.w, inv);
+            reinterpret_cast<uint2 *>(q)[j4] = make_uint2(a | (b << 16), c | (d << 16));
+            reinterpret_cast<uint32_t *>(hi)[j4] = (a >> 8) | ((b >> 8) << 8) | ((c >> 8) << 16) | ((d >> 8) << 24);
+            reinterpret_cast<uint32_t *>(lo)[j4] = (a & 255u) | ((b & 255u) << 8) | ((c & 255u) << 16) | (d << 24);
+        }
+    } else {
+        for (int j = threadIdx.x; j < H; j += blockDim.x) q[j] = quant_one(ts[j], scratch[j / g]);
+    }
     __syncthreads();
 }
 
@@ -69,7 +83,7 @@ __device__ __forceinline__ void cta_quantize_smem_row(const float *ts, int H, in
 __device__ __forceinline__ void cta_norm_quant_row(const float *x, const int8_t *wq, const float *ws, int ngs,
                                                    float eps, bool inplace_form, float *out, int16_t *q,
                                                    float *qs, int qg, int H, float *xs, float *ts,
-                                                   float *scratch) {
+                                                   float *scratch, int8_t *hi = nullptr, uint8_t *lo = nullptr) {
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x)
         reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(x) + i);
     __syncthreads();
@@ -89,7 +103,7 @@ __device__ __forceinline__ void cta_norm_quant_row(const float *x, const int8_t 
         __syncthreads();
         src = ts;
     }
-    if (q) cta_quantize_smem_row(src, H, qg, q, qs, scratch);
+    if (q) cta_quantize_smem_row(src, H, qg, q, qs, scratch, hi, lo);
 }
 
 // Fused tail of a producer kernel: the last CTA of the grid to finish runs

@@ -31,7 +31,8 @@ import torch
 from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Workspace, attention, embedding_lookup_i8,
                attention_ordered, DECODE_REFERENCE_ORDER,
                attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
-               qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct)
+               qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct,
+               Planes, linear_planes_batched, quantize_rows_planes, rms_norm_i8_planes)
 from . import load_library
 from . import swiglu as swiglu_
 
@@ -183,7 +184,8 @@ class TextDecoder:
         self.use_tc = batch_order == "tiled"
         self.tc_ws = Workspace(dev)
         if self.use_tc:
-            self.tc_ws.get(load_library().qvl_linear_q16_i8_batched_workspace_bytes(max_batch, cfg.intermediate))
+            # hi/lo planes written by the quantising kernels, read by the products
+            self.planes = Planes(max_batch, max(cfg.hidden, cfg.intermediate), dev)
         self.ws = Workspace(dev)
         self.ws.get(load_library().qvl_attention_workspace_bytes(B, max_ctx, self.kv[0].dims))
         if attn_order == "reference":
@@ -278,33 +280,33 @@ class TextDecoder:
 
     def _step_tc(self, B):
         """Tensor-core batch (reference M>1 order): every linear runs as one
-        M=B tcgen05 product; activations are split into hi/lo planes once per
-        distinct input."""
+        M=B tcgen05 product; the kernels that quantise an activation row also
+        write its hi/lo planes, and q/k/v and gate/up are one launch each."""
         cfg, t = self.cfg, self.w.t
-        H, ng, eps = cfg.hidden, cfg.norm_group, cfg.eps
+        H, I, ng, eps = cfg.hidden, cfg.intermediate, cfg.norm_group, cfg.eps
         x, qx, qx_s = self.x[:B], self.qx[:B], self.qx_s[:B]
         seq, pos = self.seq_ids[:B], self.positions[:B]
-        ws = self.tc_ws
+        P = self.planes
+        acc = SEM_TILED | SEM_ACCUMULATE
         for l in range(cfg.layers):
-            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
-            linear_batched(qx, qx_s, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
-                           [self.q[:B], self.k[:B], self.v[:B]], ws)
+            rms_norm_i8_planes(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, qx, qx_s, P)
+            linear_planes_batched(P, qx_s, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
+                                  [self.q[:B], self.k[:B], self.v[:B]], B, H)
             qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
-            (attention_ordered if self.attn_order == "reference" else attention)(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
-            _quantize_into(self.att[:B], self.qa[:B], self.qa_s[:B])
-            linear_batched(self.qa[:B], self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], ws,
-                           semantics=SEM_TILED | SEM_ACCUMULATE)
-            rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qx, q_scales=qx_s, quant_group=H)
-            linear_batched(qx, qx_s, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
-                           [self.gate[:B], self.up[:B]], ws, swiglu_pair=True, up_scratch=self.up[:B])
-            _quantize_into(self.gate[:B], self.qh[:B], self.qh_s[:B])
-            linear_batched(self.qh[:B], self.qh_s[:B], [(t["wd"][l], t["wd_s"][l])], [x], ws,
-                           semantics=SEM_TILED | SEM_ACCUMULATE)
-        rms_norm_i8(x, t["final_norm"], t["final_norm_s"], ng, eps, out=x, q=qx, q_scales=qx_s, quant_group=H,
-                    inplace_form=True)
-        linear_batched(qx, qx_s, [(t["embed"], t["embed_s"])], [self.logits[:B]], ws)
+            (attention_ordered if self.attn_order == "reference" else attention)(
+                self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+            quantize_rows_planes(self.att[:B], self.qa[:B], self.qa_s[:B], P)
+            linear_planes_batched(P, self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], B, H, semantics=acc)
+            rms_norm_i8_planes(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, qx, qx_s, P)
+            linear_planes_batched(P, qx_s, [(t["wg"][l], t["wg_s"][l]), (t["wu"][l], t["wu_s"][l])],
+                                  [self.gate[:B], self.up[:B]], B, H)
+            swiglu_(self.gate[:B], self.up[:B])
+            quantize_rows_planes(self.gate[:B], self.qh[:B], self.qh_s[:B], P)
+            linear_planes_batched(P, self.qh_s[:B], [(t["wd"][l], t["wd_s"][l])], [x], B, I, semantics=acc)
+        rms_norm_i8_planes(x, t["final_norm"], t["final_norm_s"], ng, eps, qx, qx_s, P, out=x, inplace_form=True)
+        linear_planes_batched(P, qx_s, [(t["embed"], t["embed_s"])], [self.logits[:B]], B, H)
 
     def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0, image_embeds=None, deepstack=None,
                 image_token_id: int = 151655, order: str = "tiled"):
@@ -342,6 +344,7 @@ class TextDecoder:
                       seq=torch.zeros(T, dtype=torch.int32, device=dev),
                       pos=torch.zeros(T, dtype=torch.int32, device=dev), ws=Workspace(dev))
             pf["ws"].get(load_library().qvl_linear_q16_i8_batched_workspace_bytes(T, I))
+            pf["planes"] = Planes(T, I, dev)
             self._pf = pf
         x, q16, qs = pf["x"][:T], pf["q16"][:T], pf["qs"][:T]
         qh = pf["qh"][:T]
@@ -364,19 +367,42 @@ class TextDecoder:
         attn = attention_ordered if self.attn_order == "reference" else attention
         if self.attn_order == "reference":
             ws.get(load_library().qvl_attention_ordered_workspace_bytes(T, self.max_ctx, self.kv[0].dims))
+        # one process, tensor-core order: the quantising kernels write the
+        # products' hi/lo planes, q/k/v and gate/up are one launch each
+        planes = pf["planes"] if (not lane8 and self.tp is None) else None
+        accs = SEM_TILED | SEM_ACCUMULATE
+
+        def mats(names, l):
+            return [(t[n][l], t[n + "_s"][l]) for n in names]
+
         for l in range(cfg.layers):
-            rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
-            prod(qh, qs, ("wq", "wk", "wv"), l, [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
+            if planes is not None:
+                rms_norm_i8_planes(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, qh, qs, planes)
+                linear_planes_batched(planes, qs, mats(("wq", "wk", "wv"), l), [pf["q"][:T], pf["k"][:T], pf["v"][:T]],
+                                      T, H)
+            else:
+                rms_norm_i8(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
+                prod(qh, qs, ("wq", "wk", "wv"), l, [pf["q"][:T], pf["k"][:T], pf["v"][:T]], ws)
             qknorm_rope_kv_append(pf["q"][:T], pf["k"][:T], pf["v"][:T], self.kv[l], sq, ps, self.rope_cos,
                                   self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
                                   t["k_norm_s"][l], ng, eps)
             attn(pf["q"][:T], self.kv[l], sq, ps, self.max_ctx, out=pf["att"][:T], workspace=ws)
-            _quantize_into(pf["att"][:T], qh, qs)
-            prod(qh, qs, ("wo",), l, [x], ws, acc=True)
-            rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
-            prod(qh, qs, ("wg", "wu"), l, [pf["gate"][:T], pf["up"][:T]], ws, swiglu=True, up_scratch=pf["up"][:T])
-            _quantize_into(pf["gate"][:T], q16, qs)
-            prod(q16, qs, ("wd",), l, [x], ws, acc=True)
+            if planes is not None:
+                quantize_rows_planes(pf["att"][:T], qh, qs, planes)
+                linear_planes_batched(planes, qs, mats(("wo",), l), [x], T, H, semantics=accs)
+                rms_norm_i8_planes(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, qh, qs, planes)
+                linear_planes_batched(planes, qs, mats(("wg", "wu"), l), [pf["gate"][:T], pf["up"][:T]], T, H)
+                swiglu_(pf["gate"][:T], pf["up"][:T])
+                quantize_rows_planes(pf["gate"][:T], q16, qs, planes)
+                linear_planes_batched(planes, qs, mats(("wd",), l), [x], T, I, semantics=accs)
+            else:
+                _quantize_into(pf["att"][:T], qh, qs)
+                prod(qh, qs, ("wo",), l, [x], ws, acc=True)
+                rms_norm_i8(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, q=qh, q_scales=qs, quant_group=H)
+                prod(qh, qs, ("wg", "wu"), l, [pf["gate"][:T], pf["up"][:T]], ws, swiglu=True,
+                     up_scratch=pf["up"][:T])
+                _quantize_into(pf["gate"][:T], q16, qs)
+                prod(q16, qs, ("wd",), l, [x], ws, acc=True)
             if img_rows is not None and l < deepstack.shape[0]:
                 # add_vector(x, deep-stack row): fp32 x + the fp16 value
                 x[img_rows] += deepstack[l, :img_rows.numel()].to(torch.float32)
@@ -479,6 +505,10 @@ class TextDecoder:
     def kernels_per_step(self):
         if self.persistent:
             return 1
+        if self.use_tc:
+            # norm, q/k/v, rope, attention (2 in the reference order), quantise, o,
+            # norm, gate/up, swiglu, quantise, down; embedding, final norm, LM head, argmax
+            return 1 + self.cfg.layers * (11 + (2 if self.attn_order == "reference" else 1)) + 3
         return 1 + self.cfg.layers * (1 + 1 + 1 + 3 + 1 + 1 + 1 + 1 + 1 + 1) + 1 + 1 + 1
 
 

@@ -418,3 +418,66 @@ def test_attention_with_fused_quantisation(qvl, cuda, ctxs):
     assert torch.equal(out, ref)
     assert torch.equal(q16, rq) and torch.equal(s16, rs)
     assert int(counter.item()) == 0
+
+
+@pytest.mark.parametrize("M,K", [(32, 2048), (452, 6144), (16, 1024)])
+def test_quantize_rows_planes(qvl, cuda, M, K):
+    """The quantisation that also writes the tensor-core planes: q and the
+    scales equal quantize_rows, hi = q >> 8 and lo = q & 255 exactly."""
+    x = np.random.default_rng(M + K).standard_normal((M, K), dtype=np.float32)
+    q0, s0 = qvl.quantize_rows(dev(x, cuda), K)
+    q = torch.empty((M, K), dtype=torch.int16, device=cuda)
+    s = torch.empty((M, 1), dtype=torch.float32, device=cuda)
+    P = qvl.Planes(M, K, cuda)
+    qvl.quantize_rows_planes(dev(x, cuda), q, s, P)
+    np.testing.assert_array_equal(q.cpu().numpy(), q0.cpu().numpy())
+    np.testing.assert_array_equal(s.cpu().numpy(), s0.cpu().numpy())
+    qn = q.cpu().numpy().astype(np.int32).reshape(-1)
+    np.testing.assert_array_equal(P.hi.cpu().numpy()[:M * K].astype(np.int32), qn >> 8)
+    np.testing.assert_array_equal(P.lo.cpu().numpy()[:M * K].astype(np.int32), qn & 255)
+
+
+def test_rms_norm_planes_matches_rms_norm(qvl, cuda):
+    M, H, ng = 32, 2048, 128
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((M, H), dtype=np.float32)
+    w = rng.integers(-127, 128, H, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, H // ng).astype(np.float32)
+    q0 = torch.empty((M, H), dtype=torch.int16, device=cuda)
+    s0 = torch.empty((M, 1), dtype=torch.float32, device=cuda)
+    qvl.rms_norm_i8(dev(x, cuda), dev(w, cuda), dev(ws, cuda), ng, 1e-6, q=q0, q_scales=s0, quant_group=H)
+    q = torch.empty_like(q0)
+    s = torch.empty_like(s0)
+    P = qvl.Planes(M, H, cuda)
+    qvl.rms_norm_i8_planes(dev(x, cuda), dev(w, cuda), dev(ws, cuda), ng, 1e-6, q, s, P)
+    np.testing.assert_array_equal(q.cpu().numpy(), q0.cpu().numpy())
+    np.testing.assert_array_equal(s.cpu().numpy(), s0.cpu().numpy())
+    qn = q.cpu().numpy().astype(np.int32).reshape(-1)
+    np.testing.assert_array_equal(P.hi.cpu().numpy().astype(np.int32), qn >> 8)
+    np.testing.assert_array_equal(P.lo.cpu().numpy().astype(np.int32), qn & 255)
+
+
+@pytest.mark.parametrize("M,acc", [(32, False), (452, False), (32, True)])
+def test_linear_planes_batched_three_matrices(qvl, cuda, M, acc):
+    """q/k/v-shaped products of one set of planes in a single launch (weight
+    tiles of the three matrices numbered one after the other), TILED order,
+    bit-exact; with acc, C += product."""
+    K = 2048
+    rng = np.random.default_rng(M + 3)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    Ns = (2048, 1024, 1024)
+    ws_ = [rng.integers(-127, 128, (n, K), dtype=np.int8) for n in Ns]
+    ss = [rng.uniform(0.001, 0.02, n).astype(np.float32) for n in Ns]
+    c0 = [rng.standard_normal((M, n), dtype=np.float32) for n in Ns]
+    q = torch.empty((M, K), dtype=torch.int16, device=cuda)
+    s = torch.empty((M, 1), dtype=torch.float32, device=cuda)
+    P = qvl.Planes(M, K, cuda)
+    qvl.quantize_rows_planes(dev(x, cuda), q, s, P)
+    outs = [dev(c.copy(), cuda) if acc else torch.empty((M, n), device=cuda) for c, n in zip(c0, Ns)]
+    qvl.linear_planes_batched(P, s, [(dev(w, cuda), dev(sc, cuda)) for w, sc in zip(ws_, ss)], outs, M, K,
+                              semantics=qvl.SEM_TILED | (qvl.SEM_ACCUMULATE if acc else 0))
+    for o, w, sc, c in zip(outs, ws_, ss, c0):
+        want = oracle.linear_i8(x, w, sc, K, oracle.TILED, threads=16)
+        if acc:
+            want = (c + want).astype(np.float32)
+        np.testing.assert_array_equal(o.cpu().numpy(), want)
