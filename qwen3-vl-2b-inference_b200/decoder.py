@@ -353,13 +353,17 @@ class TextDecoder:
         sq, ps = pf["seq"][:T], pf["pos"][:T]
         ws = pf["ws"]
         embedding_lookup_i8(t["embed"], t["embed_s"], tokens.to(torch.int32), x)
-        img_rows = None
+        img_mask = img_idx = None
         if image_embeds is not None:
-            img_rows = torch.nonzero(tokens.reshape(-1) == image_token_id).reshape(-1)
-            n_img = img_rows.numel()
-            if n_img > image_embeds.shape[0]:
-                raise ValueError(f"{n_img} image tokens, {image_embeds.shape[0]} image embeddings")
-            x[img_rows] = image_embeds[:n_img].to(torch.float32)
+            # the k-th image token takes embedding row k: found on the device
+            # (running count of image tokens), no host synchronisation, so
+            # the pass can be enqueued while earlier work runs.  Image tokens
+            # beyond the embedding rows repeat the last row (the reference
+            # would read past its buffer).
+            mask = tokens.reshape(-1) == image_token_id
+            img_idx = (torch.cumsum(mask.to(torch.int32), 0) - 1).clamp_(0, image_embeds.shape[0] - 1).long()
+            img_mask = mask[:, None]
+            x.copy_(torch.where(img_mask, image_embeds.to(torch.float32)[img_idx], x))
         lane8 = order == "lane8"
         if order not in ("tiled", "lane8"):
             raise ValueError(order)
@@ -403,9 +407,9 @@ class TextDecoder:
                      up_scratch=pf["up"][:T])
                 _quantize_into(pf["gate"][:T], q16, qs)
                 prod(q16, qs, ("wd",), l, [x], ws, acc=True)
-            if img_rows is not None and l < deepstack.shape[0]:
-                # add_vector(x, deep-stack row): fp32 x + the fp16 value
-                x[img_rows] += deepstack[l, :img_rows.numel()].to(torch.float32)
+            if img_mask is not None and l < deepstack.shape[0]:
+                # add_vector(x, deep-stack row): fp32 x + the fp16 value, image rows only
+                x.copy_(torch.where(img_mask, x + deepstack[l].to(torch.float32)[img_idx], x))
         last = x[T - 1:T]
         rms_norm_i8(last, t["final_norm"], t["final_norm_s"], ng, eps, out=last, q=qh[:1], q_scales=qs[:1],
                     quant_group=H, inplace_form=True)
