@@ -188,6 +188,7 @@ int qvl_swiglu(float *gate, const float *up, size_t n, void *stream);
 int qvl_swiglu_quantize_rows(const float *gate, const float *up, int16_t *q, float *q_scales,
                              size_t M, size_t I, size_t group_size, void *stream);
 
+
 /* Fused MLP chain: out[M,H] = down(swiglu(gate(x), up(x))), the sequence of
  * model/src/forward.cpp:621-654 (gate/up linear, swiglu, down linear).
  * Wg, Wu: int8 [I, H]; Wd: int8 [H, I]; scales in the reference layout.
@@ -263,6 +264,23 @@ int qvl_attention_decode_ordered(const float *q, const uint16_t *k_pages, const 
                                  const int32_t *positions, size_t nq, int max_ctx, float *out,
                                  const qvl_attn_dims *dims, void *workspace,
                                  size_t workspace_bytes, void *stream);
+
+/* One decode step's QK-norm + RoPE + KV append (qvl_qknorm_rope_kv_append,
+ * model/src/forward.cpp:531-562) fused into qvl_attention_decode_ordered
+ * (layers/src/text_layer.cpp:436-710): q fp32 [nq, NH, D], k_new/v_new fp32
+ * [nq, NKV, D] are the raw projections (q is not modified); k (rotated) and v
+ * are rounded to fp16 and written at each query's position, and out equals
+ * qvl_qknorm_rope_kv_append followed by qvl_attention_decode_ordered bit for
+ * bit.  Every query must belong to a different sequence (a decode batch);
+ * max_ctx <= dims->max_pos.  q_norm_w NULL: no QK-norm (all four NULL).
+ * Workspace as qvl_attention_decode_ordered. */
+int qvl_qknorm_rope_attention_decode_ordered(const float *q, const float *k_new, const float *v_new, uint16_t *k_pages,
+                                             uint16_t *v_pages, const int32_t *page_table, const int32_t *seq_ids,
+                                             const int32_t *positions, size_t nq, int max_ctx, const float *rope_cos,
+                                             const float *rope_sin, const int8_t *q_norm_w, const float *q_norm_s,
+                                             const int8_t *k_norm_w, const float *k_norm_s, size_t norm_group,
+                                             float eps, float *out, const qvl_attn_dims *dims, void *workspace,
+                                             size_t workspace_bytes, void *stream);
 
 /* qvl_attention_decode followed by the activation quantisation of each
  * output row (one scale per row, the o_proj input): q_out int16 [nq, NH*D],

@@ -50,7 +50,7 @@ EXPORTED = (
     "qvl_text_decode_step_ex",
     "qvl_text_decode_abort_flag", "qvl_text_decode_trace", "qvl_tc_timeout_status",
     "qvl_attention_decode_static", "qvl_attention_ordered_workspace_bytes", "qvl_attention_decode_ordered",
-    "qvl_rope_table", "qvl_quantize_rows_planes", "qvl_rms_norm_i8_planes", "qvl_linear_planes_i8_batched",
+    "qvl_rope_table", "qvl_quantize_rows_planes", "qvl_qknorm_rope_attention_decode_ordered", "qvl_rms_norm_i8_planes", "qvl_linear_planes_i8_batched",
 )
 SEM_ACCUMULATE = 0x100
 
@@ -140,6 +140,8 @@ def load_library(path: str = LIB_PATH):
     L.qvl_tc_timeout_status.argtypes = [ctypes.POINTER(_I), _I, _P]
     L.qvl_rope_table.argtypes = [_I, _I, _I, _P, _P]
     L.qvl_quantize_rows_planes.argtypes = [_P] * 5 + [_Z, _Z, _Z, _P]
+    L.qvl_qknorm_rope_attention_decode_ordered.argtypes = ([_P] * 8 + [_Z, _I] + [_P] * 6 +
+                                                           [_Z, ctypes.c_float, _P, _P, _P, _Z, _P])
     L.qvl_rms_norm_i8_planes.argtypes = [_P] * 8 + [_Z, _Z, _Z, ctypes.c_float, _I, _P]
     L.qvl_linear_planes_i8_batched.argtypes = [_P, _P, _P, _Z, _P, _P, _P, _P, _Z, _Z, _I, _P]
     L.qvl_internal_set_tc_timeout.argtypes = [_P]
@@ -318,6 +320,24 @@ def attention_ordered(q, kv: PagedKV, seq_ids, positions, max_ctx, out=None, wor
                                           _ptr(seq_ids), _ptr(positions), nq, max_ctx, _ptr(out),
                                           ctypes.byref(kv.dims), _ptr(ws), ws.numel(), _stream(stream)),
            "attention_ordered")
+    return out
+
+
+def qknorm_rope_attention_ordered(q, k_new, v_new, kv: PagedKV, seq_ids, positions, max_ctx, rope_cos, rope_sin,
+                                  q_norm_w, q_norm_s, k_norm_w, k_norm_s, norm_group, eps, out=None, workspace=None,
+                                  stream=None):
+    """qknorm_rope_kv_append + attention_ordered of one decode step in one
+    pass (q is left unrotated); every query a different sequence."""
+    nq = q.shape[0]
+    if out is None:
+        out = torch.empty_like(q)
+    L = load_library()
+    ws = _ws(workspace, q.device).get(L.qvl_attention_ordered_workspace_bytes(nq, max_ctx, ctypes.byref(kv.dims)))
+    _check(L.qvl_qknorm_rope_attention_decode_ordered(
+        _ptr(q), _ptr(k_new), _ptr(v_new), kv.k.data_ptr(), kv.v.data_ptr(), _ptr(kv.page_table), _ptr(seq_ids),
+        _ptr(positions), nq, max_ctx, _ptr(rope_cos), _ptr(rope_sin), _ptr(q_norm_w), _ptr(q_norm_s),
+        _ptr(k_norm_w), _ptr(k_norm_s), norm_group, eps, _ptr(out), ctypes.byref(kv.dims), _ptr(ws), ws.numel(),
+        _stream(stream)), "qknorm_rope_attention_ordered")
     return out
 
 

@@ -49,12 +49,19 @@ constexpr int kKRow = kD * 2 + 16;     // staged key row: 256 B + 16 B of paddin
 // head's query rows (kv_mul * 128 floats), then the block's 128 key rows.
 // The key rows are staged with contiguous 16-byte cp.async copies (16
 // threads per row) and each thread then reads its own row from shared memory.
-template <int KVM>
-__global__ void __launch_bounds__(kThreads)
+// ROPE: the query rows are the raw q/k/v projections of a decode step (one
+// query per sequence).  Every CTA applies the QK-norm and RoPE of its KV
+// head's query heads itself (rope_append_kernel's arithmetic, attention.cu);
+// the CTA whose block holds the query's position also normalises and rotates
+// the new key, appends key and value to the pages as fp16 and puts the key
+// row straight into its staging area.  One launch less per layer; the cache
+// row at the position is not read before it is written.
+template <int KVM, bool ROPE>
+__global__ void __launch_bounds__(kThreads, 6)
 attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict k_pages,
                            const int32_t *__restrict page_table, const int32_t *__restrict seq_ids,
                            const int32_t *__restrict positions, float *__restrict scores, int max_ctx, int NH,
-                           int NKV, int P, int maxp) {
+                           int NKV, int P, int maxp, OrdRope rp) {
     extern __shared__ __align__(16) float qs[];
     pdl_launch_dependents();
     pdl_wait();
@@ -63,19 +70,82 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
     const int pos = positions[i];
     const int t0 = blockIdx.x * kThreads;
     if (pos < 0 || pos >= max_ctx || t0 > pos) return;
-    unsigned char *ks = reinterpret_cast<unsigned char *>(qs + kvm * kD);
+    const bool owner = ROPE && pos < t0 + kThreads;     // this block holds the new position
+    float *kraw = qs + kvm * kD;                          // ROPE: the new key row
+    unsigned char *ks = reinterpret_cast<unsigned char *>(qs + (ROPE ? kvm + 1 : kvm) * kD);
     const int32_t *pt_row = page_table + (size_t)seq_ids[i] * maxp;
     const int rows = min(kThreads, pos + 1 - t0);
     __shared__ size_t rowoff[kThreads];     // 16-byte index of each staged key row (one page lookup per row)
     if (threadIdx.x < rows) rowoff[threadIdx.x] = kv_index(pt_row, t0 + threadIdx.x, kvh, NKV, P) / 8;
     __syncthreads();
     const uint4 *kp = reinterpret_cast<const uint4 *>(k_pages);
-    for (int e = threadIdx.x; e < rows * 16; e += kThreads) {
+    const int staged = owner ? rows - 1 : rows;           // the position's row comes from registers
+    for (int e = threadIdx.x; e < staged * 16; e += kThreads) {
         const int r = e >> 4, c = e & 15;
         cp_async16(ks + r * kKRow + c * 16, kp + rowoff[r] + c);
     }
     cp_async_commit();
     for (int e = threadIdx.x; e < kvm * kD; e += blockDim.x) qs[e] = q[((size_t)i * NH + kvh * kvm) * kD + e];
+    if constexpr (ROPE) {
+        constexpr int half = kD / 2;
+        const int nr = owner ? kvm + 1 : kvm;             // rows to normalise and rotate
+        if (owner) {
+            kraw[threadIdx.x] = rp.k_new[((size_t)i * NKV + kvh) * kD + threadIdx.x];
+            const size_t off = rowoff[pos - t0] * 8 + threadIdx.x;
+            rp.v_pages[off] = __half_as_ushort(__float2half_rn(rp.v_new[((size_t)i * NKV + kvh) * kD + threadIdx.x]));
+        }
+        __syncthreads();
+        if (rp.norm.q_w) {
+            __shared__ float red[(KVM + 1) * 8];
+            __shared__ float invh[KVM + 1];
+            if (threadIdx.x < nr * 8) {
+                const int h = threadIdx.x >> 3, l = threadIdx.x & 7;
+                const float *xh = qs + h * kD;
+                float acc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < kD; j += 8) acc = add_rn(acc, mul_rn(xh[j + l], xh[j + l]));
+                red[threadIdx.x] = acc;
+            }
+            __syncthreads();
+            if (threadIdx.x < nr) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int l = 0; l < 8; ++l) ss = add_rn(ss, red[threadIdx.x * 8 + l]);
+                const float a = fma_rn(ss, __fdiv_rn(1.0f, (float)kD), rp.norm.eps);
+                invh[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(a));
+            }
+            __syncthreads();
+            for (int e = threadIdx.x; e < nr * kD; e += blockDim.x) {
+                const int h = e / kD, j = e - h * kD;
+                const bool isq = h < kvm;
+                const int8_t *w = isq ? rp.norm.q_w : rp.norm.k_w;
+                const float *ws = isq ? rp.norm.q_s : rp.norm.k_s;
+                qs[e] = mul_rn((float)w[j], mul_rn(mul_rn(ws[j / rp.norm.gs], invh[h]), qs[e]));
+            }
+            __syncthreads();
+        }
+        const float *c = rp.rope_cos + (size_t)pos * half;
+        const float *sn = rp.rope_sin + (size_t)pos * half;
+        for (int e = threadIdx.x; e < nr * half; e += blockDim.x) {
+            const int h = e / half, j = e - h * half;
+            float *x = qs + h * kD;
+            const float x1 = x[j], x2 = x[j + half];
+            const float y1 = fma_rn(x1, c[j], -mul_rn(x2, sn[j]));
+            const float y2 = fma_rn(x1, sn[j], mul_rn(x2, c[j]));
+            if (h < kvm) {
+                x[j] = y1;
+                x[j + half] = y2;
+            } else {
+                const uint16_t k1 = __half_as_ushort(__float2half_rn(y1)), k2 = __half_as_ushort(__float2half_rn(y2));
+                const size_t off = rowoff[pos - t0] * 8;
+                rp.k_pages[off + j] = k1;
+                rp.k_pages[off + j + half] = k2;
+                uint16_t *kr = reinterpret_cast<uint16_t *>(ks + (pos - t0) * kKRow);
+                kr[j] = k1;
+                kr[j + half] = k2;
+            }
+        }
+    }
     cp_async_wait<0>();
     __syncthreads();
     const int t = t0 + threadIdx.x;
@@ -328,7 +398,7 @@ size_t attn_ordered_workspace_bytes(size_t nq, int max_ctx, int NH) {
     return ((nq * (size_t)NH * (size_t)max_ctx * sizeof(float)) + 255) & ~(size_t)255;
 }
 
-cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStream_t stream) {
+cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStream_t stream, const OrdRope *rope) {
     float *scores = static_cast<float *>(workspace);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -339,18 +409,26 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
     cfg.stream = stream;
     cfg.gridDim = dim3((a.max_ctx + kThreads - 1) / kThreads, a.NKV, (unsigned)a.nq);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)(a.NH / a.NKV) * kD * sizeof(float) + (size_t)kThreads * kKRow;
+    cfg.dynamicSmemBytes = (size_t)(a.NH / a.NKV + (rope ? 1 : 0)) * kD * sizeof(float) + (size_t)kThreads * kKRow;
     const int kvm = a.NH / a.NKV;
+    const OrdRope rp = rope ? *rope : OrdRope{};
     auto sc = [&](auto kern) {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)cfg.dynamicSmemBytes);
         if (e2 != cudaSuccess) return e2;
         return cudaLaunchKernelEx(&cfg, kern, a.q, a.k_pages, a.page_table, a.seq_ids, a.positions, scores,
-                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp, rp);
     };
-    cudaError_t e = kvm == 1 ? sc(attn_ordered_scores_kernel<1>)
-                  : kvm == 2 ? sc(attn_ordered_scores_kernel<2>)
-                  : kvm == 4 ? sc(attn_ordered_scores_kernel<4>) : cudaErrorInvalidValue;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (rope) {
+        e = kvm == 1 ? sc(attn_ordered_scores_kernel<1, true>)
+          : kvm == 2 ? sc(attn_ordered_scores_kernel<2, true>)
+          : kvm == 4 ? sc(attn_ordered_scores_kernel<4, true>) : cudaErrorInvalidValue;
+    } else {
+        e = kvm == 1 ? sc(attn_ordered_scores_kernel<1, false>)
+          : kvm == 2 ? sc(attn_ordered_scores_kernel<2, false>)
+          : kvm == 4 ? sc(attn_ordered_scores_kernel<4, false>) : cudaErrorInvalidValue;
+    }
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(a.NKV, (unsigned)a.nq);
     auto pv = [&](auto kern, size_t smem) {

@@ -685,6 +685,40 @@ int qvl_attention_decode_ordered(const float *q, const uint16_t *k_pages, const 
     return QVL_OK;
 }
 
+int qvl_qknorm_rope_attention_decode_ordered(const float *q, const float *k_new, const float *v_new, uint16_t *k_pages,
+                                             uint16_t *v_pages, const int32_t *page_table, const int32_t *seq_ids,
+                                             const int32_t *positions, size_t nq, int max_ctx, const float *rope_cos,
+                                             const float *rope_sin, const int8_t *q_norm_w, const float *q_norm_s,
+                                             const int8_t *k_norm_w, const float *k_norm_s, size_t norm_group,
+                                             float eps, float *out, const qvl_attn_dims *dims, void *workspace,
+                                             size_t workspace_bytes, void *stream) {
+    int rc = check_attn_dims(dims);
+    if (rc) return rc;
+    if (!q || !k_new || !v_new || !k_pages || !v_pages || !page_table || !seq_ids || !positions || !out ||
+        !rope_cos || !rope_sin)
+        return QVL_ERR_INVALID;
+    const bool has_norm = q_norm_w != nullptr;
+    if (has_norm && (!q_norm_s || !k_norm_w || !k_norm_s)) return QVL_ERR_INVALID;
+    if (has_norm && (norm_group == 0 || 128 % norm_group)) return QVL_ERR_UNSUPPORTED;
+    if (max_ctx <= 0 || max_ctx > dims->max_pos) return QVL_ERR_INVALID;
+    if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(q, 16)) return QVL_ERR_INVALID;
+    if (nq == 0) return QVL_OK;
+    if (nq > 65535) return QVL_ERR_UNSUPPORTED;
+    const size_t need = qvl::attn_ordered_workspace_bytes(nq, max_ctx, dims->num_heads);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return QVL_ERR_WORKSPACE;
+    qvl::AttnArgs a = {};
+    a.q = q; a.k_pages = k_pages; a.v_pages = v_pages; a.page_table = page_table;
+    a.seq_ids = seq_ids; a.positions = positions; a.nq = nq; a.max_ctx = max_ctx; a.out = out;
+    a.NH = dims->num_heads; a.NKV = dims->num_kv_heads; a.P = dims->page_size;
+    a.maxp = dims->max_pages_per_seq; a.max_pos = dims->max_pos;
+    qvl::OrdRope rp = {};
+    rp.k_new = k_new; rp.v_new = v_new; rp.k_pages = k_pages; rp.v_pages = v_pages;
+    rp.rope_cos = rope_cos; rp.rope_sin = rope_sin;
+    rp.norm = qvl::QkNorm{q_norm_w, q_norm_s, k_norm_w, k_norm_s, has_norm ? (int)norm_group : 1, eps};
+    QVL_CUDA_TRY(qvl::launch_attention_ordered(a, workspace, (cudaStream_t)stream, &rp));
+    return QVL_OK;
+}
+
 int qvl_attention_decode_q16(const float *q, const uint16_t *k_pages, const uint16_t *v_pages,
                              const int32_t *page_table, const int32_t *seq_ids, const int32_t *positions,
                              size_t nq, int max_ctx, float *out, int16_t *q_out, float *q_out_scales,

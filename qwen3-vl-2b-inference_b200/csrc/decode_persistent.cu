@@ -554,6 +554,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }
         }
         GRID_WAIT_OR_EXIT();
+        if (l == 5) DETAIL_ALL(760);
 
         // ---- attention, phase 1.  q/k rms_norm_inplace + RoPE of this KV
         // head's two query heads (every slice CTA of the head, redundantly)
@@ -974,6 +975,7 @@ decode_persistent_kernel(PersistWeights W, PersistState S) {
             }   // fast order
         }
         SYNC_OR_EXIT();
+        if (l == 5) DETAIL_ALL(600);
 
         // ---- attention output (combined above) -> quantisation -> o_proj + residual
         for (int i = threadIdx.x; i < H / 4; i += kPThreads)

@@ -32,7 +32,8 @@ from . import (SEM_ACCUMULATE, SEM_LANE8, SEM_TILED, PagedKV, linear_batched, Wo
                attention_ordered, DECODE_REFERENCE_ORDER,
                attention_q16, gate_up_swiglu, greedy_decode, linear_q16, linear_q16_multi, linear_tail,
                qknorm_rope_kv_append, rms_norm_i8, text_decode_step, text_decode_workspace, text_weights_struct,
-               Planes, linear_planes_batched, quantize_rows_planes, rms_norm_i8_planes)
+               Planes, linear_planes_batched, quantize_rows_planes, rms_norm_i8_planes,
+               qknorm_rope_attention_ordered)
 from . import load_library
 from . import swiglu as swiglu_
 
@@ -292,11 +293,18 @@ class TextDecoder:
             rms_norm_i8_planes(x, t["in_norm"][l], t["in_norm_s"][l], ng, eps, qx, qx_s, P)
             linear_planes_batched(P, qx_s, [(t[n][l], t[n + "_s"][l]) for n in ("wq", "wk", "wv")],
                                   [self.q[:B], self.k[:B], self.v[:B]], B, H)
-            qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
-                                  self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
-                                  t["k_norm_s"][l], ng, eps)
-            (attention_ordered if self.attn_order == "reference" else attention)(
-                self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
+            if self.attn_order == "reference":
+                # QK-norm, RoPE and the KV append inside the score pass (one
+                # request per sequence)
+                qknorm_rope_attention_ordered(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.max_ctx,
+                                              self.rope_cos, self.rope_sin, t["q_norm"][l], t["q_norm_s"][l],
+                                              t["k_norm"][l], t["k_norm_s"][l], ng, eps, out=self.att[:B],
+                                              workspace=self.ws)
+            else:
+                qknorm_rope_kv_append(self.q[:B], self.k[:B], self.v[:B], self.kv[l], seq, pos, self.rope_cos,
+                                      self.rope_sin, t["q_norm"][l], t["q_norm_s"][l], t["k_norm"][l],
+                                      t["k_norm_s"][l], ng, eps)
+                attention(self.q[:B], self.kv[l], seq, pos, self.max_ctx, out=self.att[:B], workspace=self.ws)
             quantize_rows_planes(self.att[:B], self.qa[:B], self.qa_s[:B], P)
             linear_planes_batched(P, self.qa_s[:B], [(t["wo"][l], t["wo_s"][l])], [x], B, H, semantics=acc)
             rms_norm_i8_planes(x, t["post_norm"][l], t["post_norm_s"][l], ng, eps, qx, qx_s, P)
@@ -510,9 +518,10 @@ class TextDecoder:
         if self.persistent:
             return 1
         if self.use_tc:
-            # norm, q/k/v, rope, attention (2 in the reference order), quantise, o,
-            # norm, gate/up, swiglu, quantise, down; embedding, final norm, LM head, argmax
-            return 1 + self.cfg.layers * (11 + (2 if self.attn_order == "reference" else 1)) + 3
+            # norm, q/k/v, rope + attention (reference order: 2 launches, the rope inside
+            # the score pass; else rope, attention), quantise, o, norm, gate/up, swiglu,
+            # quantise, down; embedding, final norm, LM head, argmax
+            return 1 + self.cfg.layers * 12 + 3
         return 1 + self.cfg.layers * (1 + 1 + 1 + 3 + 1 + 1 + 1 + 1 + 1 + 1) + 1 + 1 + 1
 
 

@@ -290,6 +290,39 @@ def test_attention_ordered_bit_exact(qvl, cuda, ctxs):
     np.testing.assert_array_equal(out, ref)
 
 
+@pytest.mark.parametrize("ctxs,with_norm", [([1, 128, 129, 452, 257], True), ([300, 1000], False),
+                                             ([512] * 32, True)])
+def test_qknorm_rope_attention_ordered_fused(qvl, cuda, ctxs, with_norm):
+    """QK-norm + RoPE + KV append inside the reference-order score pass equals
+    qknorm_rope_kv_append followed by attention_ordered bit for bit: the
+    attention output and every page of the cache (positions at, before and
+    after a 128-position block boundary, the first position, no QK-norm)."""
+    kv, caches, q, kn, vn, cos, sin = _attn_setup(qvl, cuda, ctxs, seed=29 + len(ctxs))
+    B, ng, eps = len(ctxs), 16, 1e-6
+    rng = np.random.default_rng(5)
+    nw = [dev(rng.integers(-127, 128, D, dtype=np.int8), cuda) if with_norm else None for _ in range(2)]
+    ns = [dev(rng.uniform(0.001, 0.02, D // ng).astype(np.float32), cuda) if with_norm else None for _ in range(2)]
+    seq = torch.arange(B, dtype=torch.int32, device=cuda)
+    pos = torch.tensor([c - 1 for c in ctxs], dtype=torch.int32, device=cuda)
+    cd, sd, knd, vnd = dev(cos, cuda), dev(sin, cuda), dev(kn, cuda), dev(vn, cuda)
+    k0, v0 = kv.k.clone(), kv.v.clone()
+    qd = dev(q, cuda)
+    if with_norm:
+        qvl.qknorm_rope_kv_append(qd, knd, vnd, kv, seq, pos, cd, sd, nw[0], ns[0], nw[1], ns[1], ng, eps)
+    else:
+        qvl.rope_kv_append(qd, knd, vnd, kv, seq, pos, cd, sd)
+    ref = qvl.attention_ordered(qd, kv, seq, pos, max(ctxs))
+    k_ref, v_ref = kv.k.clone(), kv.v.clone()
+    kv.k.copy_(k0)
+    kv.v.copy_(v0)
+    qraw = dev(q, cuda)
+    out = qvl.qknorm_rope_attention_ordered(qraw, knd, vnd, kv, seq, pos, max(ctxs), cd, sd, nw[0], ns[0], nw[1],
+                                            ns[1], ng, eps)
+    assert torch.equal(out, ref)
+    assert torch.equal(kv.k, k_ref) and torch.equal(kv.v, v_ref)
+    np.testing.assert_array_equal(qraw.cpu().numpy(), q)
+
+
 def test_attention_causal_prefill(qvl, cuda):
     """512 prompt tokens of one sequence: append all, then one causal pass."""
     T = 512
