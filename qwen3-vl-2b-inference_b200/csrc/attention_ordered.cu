@@ -216,9 +216,13 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
 
 constexpr int kSumChunk = 1024;    // exponentials staged per pass of the lane sums (per query head)
 constexpr int kPvChunk = 64;       // V rows per P.V stage (16 KB)
-constexpr int kPvStages = 4;       // stages in flight (cp.async ring)
+// stages in flight (cp.async ring): 4, or 2 when there are many queries
+// (more CTAs resident per SM outweigh the shallower ring: a 452-token
+// causal prompt pass)
+constexpr int kPvStagesMax = 4;
+constexpr int kPvManyQueries = 64;
 
-template <int KVM>
+template <int KVM, int kPvStages>
 struct PvSmem {
     static constexpr size_t kV = (size_t)kPvStages * kPvChunk * kD * 2;        // fp16 V rows
     static constexpr size_t kP = (size_t)kPvStages * KVM * kPvChunk * 4;       // probabilities (global path)
@@ -238,14 +242,14 @@ constexpr int kSmemCtx = 4096;
 // chain over t ascending.  SE: the row (n <= kSmemCtx) lives in shared
 // memory from the first read on; otherwise the exponentials are formed in
 // place in `scores` and staged in chunks.
-template <int KVM, bool SE>
+template <int KVM, bool SE, int kPvStages>
 __global__ void __launch_bounds__(KVM * kThreads)
 attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
                                const int32_t *__restrict seq_ids, const int32_t *__restrict positions,
                                float *__restrict scores, float *__restrict out, int max_ctx, int NH, int NKV,
                                int P, int maxp) {
     extern __shared__ __align__(16) unsigned char pv_smem[];
-    using L = PvSmem<KVM>;
+    using L = PvSmem<KVM, kPvStages>;
     uint4 *vbuf = reinterpret_cast<uint4 *>(pv_smem);                              // [stage][64 * 16]
     float *pbuf = reinterpret_cast<float *>(pv_smem + L::kV);                     // [stage][KVM][64]
     float *ebuf_all = reinterpret_cast<float *>(pv_smem + L::kV + L::kP);         // SE: [KVM][max_ctx]
@@ -441,15 +445,23 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
     };
     // the score rows in shared memory when they fit
     const bool se = a.max_ctx <= kSmemCtx;
-    auto se_bytes = [&](int m) { return PvSmem<1>::kV + (size_t)kPvStages * m * kPvChunk * 4 + (size_t)m * ((a.max_ctx + 3) & ~3) * 4; };
+    const bool many = a.nq >= (size_t)kPvManyQueries;
+    auto se_bytes = [&](int m, int st) {
+        return (size_t)st * kPvChunk * kD * 2 + (size_t)st * m * kPvChunk * 4 + (size_t)m * ((a.max_ctx + 3) & ~3) * 4;
+    };
     if (se) {
-        if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true>, se_bytes(1));
-        if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true>, se_bytes(2));
-        if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true>, se_bytes(4));
+        if (many) {
+            if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true, 2>, se_bytes(1, 2));
+            if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true, 2>, se_bytes(2, 2));
+            if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true, 2>, se_bytes(4, 2));
+        }
+        if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true, kPvStagesMax>, se_bytes(1, kPvStagesMax));
+        if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true, kPvStagesMax>, se_bytes(2, kPvStagesMax));
+        if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true, kPvStagesMax>, se_bytes(4, kPvStagesMax));
     }
-    if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, false>, PvSmem<1>::kBytes);
-    if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, false>, PvSmem<2>::kBytes);
-    if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, false>, PvSmem<4>::kBytes);
+    if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, false, kPvStagesMax>, PvSmem<1, kPvStagesMax>::kBytes);
+    if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, false, kPvStagesMax>, PvSmem<2, kPvStagesMax>::kBytes);
+    if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, false, kPvStagesMax>, PvSmem<4, kPvStagesMax>::kBytes);
     return cudaErrorInvalidValue;
 }
 
