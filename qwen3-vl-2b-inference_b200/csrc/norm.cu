@@ -15,24 +15,31 @@
 
 namespace qvl {
 
-// grid: rows; block 256; dynamic smem 2*H floats.
+// grid: rows; block 256; dynamic smem 2*H floats (+ H + H/ngs with stage_w).
 // out (nullable) receives the normalised row; q/qs (nullable) its
 // quantisation with group qg (bit-exact with quantize_rows on `out`).
+// The norm weight does not depend on the previous kernel: it is staged in
+// shared memory (as floats) before the programmatic-dependent-launch wait.
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const float *x, const int8_t *__restrict wq,
                      const float *__restrict ws, float *out, int16_t *__restrict q,
                      float *__restrict qs, int H, int ngs, float eps, int inplace_form, int qg,
-                     int8_t *__restrict hi, uint8_t *__restrict lo) {
+                     int8_t *__restrict hi, uint8_t *__restrict lo, int stage_w) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float scratch[65];
     pdl_launch_dependents();
+    float *wqf = stage_w ? sm + 2 * H : nullptr, *wsg = stage_w ? sm + 3 * H : nullptr;
+    if (stage_w) {
+        for (int j = threadIdx.x; j < H; j += blockDim.x) wqf[j] = (float)wq[j];
+        for (int j = threadIdx.x; j < H / ngs; j += blockDim.x) wsg[j] = ws[j];
+    }
     pdl_wait();
     const int row = blockIdx.x;
     const int G = q ? H / qg : 0;
     cta_norm_quant_row(x + (size_t)row * H, wq, ws, ngs, eps, inplace_form != 0,
                        out ? out + (size_t)row * H : nullptr, q ? q + (size_t)row * H : nullptr,
                        q ? qs + (size_t)row * G : nullptr, qg, H, sm, sm + H, scratch,
-                       hi ? hi + (size_t)row * H : nullptr, lo ? lo + (size_t)row * H : nullptr);
+                       hi ? hi + (size_t)row * H : nullptr, lo ? lo + (size_t)row * H : nullptr, wqf, wsg);
 }
 
 // grid: n_tokens; block 256.  out[t] = (float)table[id] * scale[id]
@@ -66,14 +73,16 @@ cudaError_t launch_rmsnorm_quant(const float *x, const int8_t *wq, const float *
     pdl_attr(cfg, attr, st);
     cfg.gridDim = dim3(rows);
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t)2 * H * sizeof(float);
+    const size_t staged = ((size_t)3 * H + (size_t)H / ngs) * sizeof(float);
+    const int stage_w = (wq != nullptr && staged <= 160 * 1024) ? 1 : 0;
+    cfg.dynamicSmemBytes = stage_w ? staged : (size_t)2 * H * sizeof(float);
     if (cfg.dynamicSmemBytes > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)cfg.dynamicSmemBytes);
         if (e != cudaSuccess) return e;
     }
     return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, wq, ws, out, q, qs, H, ngs, eps,
-                              inplace_form ? 1 : 0, qg, hi, lo);
+                              inplace_form ? 1 : 0, qg, hi, lo, stage_w);
 }
 
 cudaError_t launch_embedding_i8(const int8_t *table, const float *scales, const int32_t *ids, float *out,

@@ -80,10 +80,13 @@ __device__ __forceinline__ void cta_quantize_smem_row(const float *ts, int H, in
 // One row: optional RMSNorm (wq != nullptr), then optional quantisation
 // (q != nullptr).  xs/ts: shared memory of H floats each; scratch >= 65 floats.
 // Reads x with L2-coherent loads (it may have been written by other CTAs).
+// wqf/wsg (optional): the norm weight already staged in shared memory as
+// floats ((float)wq[j], and ws[g]), read instead of wq/ws.
 __device__ __forceinline__ void cta_norm_quant_row(const float *x, const int8_t *wq, const float *ws, int ngs,
                                                    float eps, bool inplace_form, float *out, int16_t *q,
                                                    float *qs, int qg, int H, float *xs, float *ts,
-                                                   float *scratch, int8_t *hi = nullptr, uint8_t *lo = nullptr) {
+                                                   float *scratch, int8_t *hi = nullptr, uint8_t *lo = nullptr,
+                                                   const float *wqf = nullptr, const float *wsg = nullptr) {
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x)
         reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(x) + i);
     __syncthreads();
@@ -96,7 +99,9 @@ __device__ __forceinline__ void cta_norm_quant_row(const float *x, const int8_t 
         __syncthreads();
         const float inv = scratch[64];
         for (int j = threadIdx.x; j < H; j += blockDim.x) {
-            const float t = mul_rn((float)wq[j], mul_rn(mul_rn(ws[j / ngs], inv), xs[j]));
+            const float w = wqf ? wqf[j] : (float)wq[j];
+            const float g = wsg ? wsg[j / ngs] : ws[j / ngs];
+            const float t = mul_rn(w, mul_rn(mul_rn(g, inv), xs[j]));
             ts[j] = t;
             if (out) out[j] = t;
         }
