@@ -220,6 +220,10 @@ constexpr int kPvChunk = 64;       // V rows per P.V stage (16 KB)
 // (more CTAs resident per SM outweigh the shallower ring: a 452-token
 // causal prompt pass)
 constexpr int kPvStagesMax = 4;
+// Few queries and short contexts (a decode batch): 5 stages, 4 in flight; the
+// shared memory (~90 KB) still lets two CTAs share an SM
+constexpr int kPvStagesDeep = 5;
+constexpr int kPvDeepCtx = 1024;
 constexpr int kPvManyQueries = 64;
 
 template <int KVM, int kPvStages>
@@ -454,6 +458,11 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
             if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true, 2>, se_bytes(1, 2));
             if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true, 2>, se_bytes(2, 2));
             if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true, 2>, se_bytes(4, 2));
+        }
+        if (a.max_ctx <= kPvDeepCtx) {
+            if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true, kPvStagesDeep>, se_bytes(1, kPvStagesDeep));
+            if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true, kPvStagesDeep>, se_bytes(2, kPvStagesDeep));
+            if (kvm == 4) return pv(attn_ordered_softmax_pv_kernel<4, true, kPvStagesDeep>, se_bytes(4, kPvStagesDeep));
         }
         if (kvm == 1) return pv(attn_ordered_softmax_pv_kernel<1, true, kPvStagesMax>, se_bytes(1, kPvStagesMax));
         if (kvm == 2) return pv(attn_ordered_softmax_pv_kernel<2, true, kPvStagesMax>, se_bytes(2, kPvStagesMax));
