@@ -271,7 +271,9 @@ int qvl_attention_decode_ordered(const float *q, const uint16_t *k_pages, const 
  * [nq, NKV, D] are the raw projections (q is not modified); k (rotated) and v
  * are rounded to fp16 and written at each query's position, and out equals
  * qvl_qknorm_rope_kv_append followed by qvl_attention_decode_ordered bit for
- * bit.  Every query must belong to a different sequence (a decode batch);
+ * bit.  Every query must belong to a different sequence (a decode batch),
+ * and the cache rows before each query's position must be complete when the
+ * call is made (the P.V pass may fetch them while the score pass still runs);
  * max_ctx <= dims->max_pos.  q_norm_w NULL: no QK-norm (all four NULL).
  * Workspace as qvl_attention_decode_ordered. */
 int qvl_qknorm_rope_attention_decode_ordered(const float *q, const float *k_new, const float *v_new, uint16_t *k_pages,

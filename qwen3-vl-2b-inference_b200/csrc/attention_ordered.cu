@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(KVM * kThreads)
 attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t *__restrict page_table,
                                const int32_t *__restrict seq_ids, const int32_t *__restrict positions,
                                float *__restrict scores, float *__restrict out, int max_ctx, int NH, int NKV,
-                               int P, int maxp) {
+                               int P, int maxp, int early) {
     extern __shared__ __align__(16) unsigned char pv_smem[];
     using L = PvSmem<KVM, kPvStages>;
     uint4 *vbuf = reinterpret_cast<uint4 *>(pv_smem);                              // [stage][64 * 16]
@@ -262,7 +262,7 @@ attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t
     __shared__ float inv_sh[KVM];
     __shared__ int zero_sh[KVM];
     pdl_launch_dependents();
-    pdl_wait();
+    if (!early) pdl_wait();
     const int kvh = blockIdx.x, i = blockIdx.y;
     const int hh = threadIdx.x / kThreads, d = threadIdx.x % kThreads;
     const int h = kvh * KVM + hh;
@@ -312,8 +312,13 @@ attn_ordered_softmax_pv_kernel(const uint16_t *__restrict v_pages, const int32_t
         }
         cp_async_commit();    // an empty group past the end keeps the wait counts uniform
     };
-#pragma unroll
-    for (int c = 0; c < kPvStages - 1; ++c) issue(c);
+    // early: the V chunks wholly before the position are issued before the
+    // programmatic-dependent-launch wait (only the previous kernel -- the score
+    // pass, which appends the row at the position -- may still be running)
+    const int pre = early ? min(kPvStages - 1, pos / kPvChunk) : 0;
+    for (int c = 0; c < pre; ++c) issue(c);
+    if (early) pdl_wait();
+    for (int c = pre; c < kPvStages - 1; ++c) issue(c);
     if constexpr (SE) {
         for (int t = d; t < n; t += kThreads) ebuf[t] = s[t];
         __syncthreads();
@@ -420,6 +425,10 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
     cfg.dynamicSmemBytes = (size_t)(a.NH / a.NKV + (rope ? 1 : 0)) * kD * sizeof(float) + (size_t)kThreads * kKRow;
     const int kvm = a.NH / a.NKV;
     const OrdRope rp = rope ? *rope : OrdRope{};
+    // one query per sequence with the rope inside the score pass (a decode
+    // step): the cache rows before each position are not written by the
+    // score pass, so the P.V pass may fetch them before its dependent-launch wait
+    const int early = rope ? 1 : 0;
     auto sc = [&](auto kern) {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)cfg.dynamicSmemBytes);
@@ -445,7 +454,7 @@ cudaError_t launch_attention_ordered(const AttnArgs &a, void *workspace, cudaStr
         cfg.blockDim = dim3(kvm * kThreads);
         cfg.dynamicSmemBytes = smem;
         return cudaLaunchKernelEx(&cfg, kern, a.v_pages, a.page_table, a.seq_ids, a.positions, scores, a.out,
-                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp);
+                                  a.max_ctx, a.NH, a.NKV, a.P, a.maxp, early);
     };
     // the score rows in shared memory when they fit
     const bool se = a.max_ctx <= kSmemCtx;
