@@ -64,7 +64,10 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
                            int NKV, int P, int maxp, OrdRope rp) {
     extern __shared__ __align__(16) float qs[];
     pdl_launch_dependents();
-    pdl_wait();
+    // ROPE (a decode step): the cached key rows before the position are
+    // complete when the call is made, so they are staged before the
+    // dependent-launch wait; the projections are read after it
+    if (!ROPE) pdl_wait();
     const int i = blockIdx.z, kvh = blockIdx.y;
     constexpr int kvm = KVM;
     const int pos = positions[i];
@@ -85,6 +88,7 @@ attn_ordered_scores_kernel(const float *__restrict q, const uint16_t *__restrict
         cp_async16(ks + r * kKRow + c * 16, kp + rowoff[r] + c);
     }
     cp_async_commit();
+    if (ROPE) pdl_wait();
     for (int e = threadIdx.x; e < kvm * kD; e += blockDim.x) qs[e] = q[((size_t)i * NH + kvh * kvm) * kD + e];
     if constexpr (ROPE) {
         constexpr int half = kD / 2;
